@@ -1,0 +1,484 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Q8-KV decode attention hot path (one JSON line on rank 0).
+
+Default workload: per GPU, 64 sequences with context lengths U[1024, 32768]
+(seeded), 16 query / 2 KV heads, head_dim 256, Q8_0 KV.  One step = quantise-and-append one new
+N(0,1) K/V token per sequence, then split-KV attention of each sequence's query over its whole
+cache.  Inputs are synthetic (device RNG; see vxg_b200/workloads.py).  Multi-GPU: one process
+per GPU, each with its own 64 sequences (weak scaling, no data-path collective); time = max over
+ranks of the device-timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|long|deltanet]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q8-KV decode attn: HBM GB/s (% of peak) and seq-steps/s at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary (profiles/*.json)."""
+    p = os.path.join(ROOT, "profiles", name)
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("traffic_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# --------------------------------------------------------------------------- clocks (NVML)
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+            0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+            0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    """Polls SM clock and clock-event reasons of this process's GPU every ~2 ms."""
+
+    def __init__(self, torch_device: int):
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            import torch
+            props = torch.cuda.get_device_properties(torch_device)
+            h = None
+            try:
+                bus = "%08X:%02X:%02X.0" % (props.pci_domain_id, props.pci_bus_id,
+                                           props.pci_device_id)
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[torch_device]) if vis else torch_device
+                h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.h = h
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # pragma: no cover - no NVML
+            self.err = str(e)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, rs))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def start(self):
+        if self.h is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self._thread:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [s[0] for s in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= int(r)
+        reasons = [n for b, n in _REASONS.items() if bits & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(mhz)}
+
+
+# --------------------------------------------------------------------------- distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def barrier_max(torch, dist, world, value: float) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(torch, dist, world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# --------------------------------------------------------------------------- our arm
+def run_decode(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    import vxg_b200
+    from vxg_b200 import workloads as wl
+
+    K, W = args.steps, args.warmup
+    ctx = vxg_b200.Context()
+    batch = wl.DecodeBatch(seed=1 + 1000 * rank)
+    lens = batch.ctx_lens()
+    n = batch.n_seq
+    E2E_W = 2
+    cap = int(lens.max()) + W + K + E2E_W + K + 8
+    pool = vxg_b200.KvQ8Pool(ctx, n, wl.HKV, wl.HD, cap)
+    wl.fill_pool_device(pool, lens, seed=7 + rank)
+    q, kn, vn = wl.decode_step_inputs_device(n, W + K, seed=11 + rank)
+    seq = torch.arange(n, dtype=torch.int32, device="cuda")
+    pos = [torch.from_numpy(lens + i).to(torch.int32).cuda() for i in range(W + K)]
+    out = torch.empty((n, wl.HQ, wl.HD), dtype=torch.float32, device="cuda")
+    for i in range(W):
+        pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=out, max_ctx=cap)
+    ctx.sync()
+    sampler = ClockSampler(local)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier(torch, dist, world)
+    ctx.set_timing(True)
+    sampler.start()
+    e0.record()
+    for i in range(W, W + K):
+        pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=out, max_ctx=cap)
+    e1.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    rc = ctx.sync()
+    ms = e0.elapsed_time(e1)
+    split_ms = ctx.split_ms_total() / K
+    ctx.set_timing(False)
+    ms_max = barrier_max(torch, dist, world, ms)
+    split_ms_max = barrier_max(torch, dist, world, split_ms)
+    barrier(torch, dist, world)
+
+    # ---- end to end through the public API with pinned host buffers ---------------------------
+    qh = ctx.pinned_empty((E2E_W + K, n, wl.HQ, wl.HD), np.float32)
+    kh = ctx.pinned_empty((E2E_W + K, n, wl.HKV, wl.HD), np.float32)
+    vh = ctx.pinned_empty((E2E_W + K, n, wl.HKV, wl.HD), np.float32)
+    hq, hk, hv = wl.decode_step_inputs_host(n, E2E_W + K, seed=13 + rank)
+    qh[...] = hq
+    kh[...] = hk
+    vh[...] = hv
+    outh = ctx.pinned_empty((n, wl.HQ, wl.HD), np.float32)
+    seq_h = ctx.pinned_empty((n,), np.int32)
+    seq_h[...] = np.arange(n, dtype=np.int32)
+    base = lens + W + K
+    pos_h = ctx.pinned_empty((E2E_W + K, n), np.int32)
+    for i in range(E2E_W + K):
+        pos_h[i] = base + i
+    for i in range(E2E_W):
+        pool.decode(seq_h, pos_h[i], qh[i], kh[i], vh[i], out=outh, max_ctx=cap)
+    barrier(torch, dist, world)
+    t0 = time.perf_counter()
+    for i in range(E2E_W, E2E_W + K):
+        pool.decode(seq_h, pos_h[i], qh[i], kh[i], vh[i], out=outh, max_ctx=cap)
+    e2e_s = time.perf_counter() - t0
+    e2e_s = barrier_max(torch, dist, world, e2e_s)
+    h2d = seq_h.nbytes + pos_h[0].nbytes + qh[0].nbytes + kh[0].nbytes + vh[0].nbytes
+    d2h = outh.nbytes
+
+    # ---- algorithmic bytes of the split-KV pass ---------------------------------------------
+    kv_bytes = np.mean([batch.kv_bytes_per_step(i) for i in range(W, W + K)])
+    q_bytes = n * wl.HQ * wl.HD * 4
+    alg_bytes = kv_bytes + q_bytes
+    peak, peak_kind = measured_peaks()
+    achieved = alg_bytes / (split_ms_max * 1e-3) / 1e9
+    step_bytes = alg_bytes + n * (wl.HQ * wl.HD * 4 + 2 * wl.HKV * wl.HD * 4 + 1088)
+
+    res = {
+        "metric": METRIC,
+        "value": n * world * K / (ms_max * 1e-3),
+        "unit": "seq-steps/s",
+        "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_max / K,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {
+            "workload": "config2: batched decode + Q8 append, 64 seqs per GPU, ctx U[1024,32768], "
+                        "16 q / 2 kv heads, head_dim 256, Q8_0 KV (34-B blocks)",
+            "seqs_per_gpu": n, "mean_ctx": float(lens.mean()), "parallelism": f"seq-shard x{world}",
+            "l2": "inputs larger than L2 (%.2f GB of KV read per step)" % (kv_bytes / 1e9),
+            "hbm_gbs_whole_step": step_bytes / (ms_max / K * 1e-3) / 1e9,
+        },
+        "roofline": {
+            "kernel": "decode_fast_split",
+            "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_kind": peak_kind,
+            "split_ms_per_launch": split_ms_max,
+            "algorithmic_bytes_per_launch": alg_bytes,
+            "traffic": profile_traffic("decode_fast_split_config2.json"),
+        },
+        "e2e": {"value": n * world * K / e2e_s, "unit": "seq-steps/s",
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": 3 * K,
+        "clocks": sampler.summary(),
+        "device_status": rc,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_decode(pool, lens, n)
+    return res
+
+
+def cpu_baseline_decode(pool, lens, n, budget_s=12.0, n_sample=8):
+    """The oracle port on this host's cores over a bounded sample: n_sample of the sequences
+    (their real caches, exported from the device), one append+attend step each, repeated until
+    ~budget_s of wall time."""
+    from oracle import oracle
+    from vxg_b200 import workloads as wl
+    rng = np.random.default_rng(99)
+    pick = np.sort(rng.choice(n, n_sample, replace=False))
+    cap = int(lens[pick].max()) + 2
+    kpool = np.zeros((n_sample, cap, wl.HKV, wl.HD // 32, 34), np.uint8)
+    vpool = np.zeros_like(kpool)
+    for j, s in enumerate(pick):
+        k, v = pool.export_blocks(int(s), 0, int(lens[s]))
+        kpool[j, :lens[s]] = k
+        vpool[j, :lens[s]] = v
+    cores = host_cores()
+    q = rng.standard_normal((n_sample, wl.HQ, wl.HD), dtype=np.float32)
+    kn = rng.standard_normal((n_sample, wl.HKV, wl.HD), dtype=np.float32)
+    vn = rng.standard_normal((n_sample, wl.HKV, wl.HD), dtype=np.float32)
+    seq = np.arange(n_sample, dtype=np.int32)
+    pos = lens[pick].astype(np.int32)
+    kflat, vflat = kpool.reshape(-1), vpool.reshape(-1)
+    reps = 0
+    t0 = time.perf_counter()
+    while True:
+        oracle.batch_decode_q8(seq, pos, q, kn, vn, kflat, vflat, cap, wl.HQ, wl.HKV, wl.HD,
+                               do_append=True, n_threads=cores)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 1000:
+            break
+    return {"value": n_sample * reps / el, "unit": "seq-steps/s", "cores": cores, "kind": "port",
+            "sample": f"{n_sample} of the 64 sequences (mean ctx {lens[pick].mean():.0f}), one "
+                      f"append+attend step each, x{reps} repetitions, {el:.1f} s"}
+
+
+def run_deltanet(args, world, rank, local):
+    """64 seqs x 32 heads, dk = dv = 128, state R+W per step."""
+    import torch
+    import torch.distributed as dist
+    import vxg_b200
+    K, W = args.steps, args.warmup
+    ctx = vxg_b200.Context()
+    B, H, D = 64, 32, 128
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5 + rank)
+    state = torch.randn((B, H, D, D), generator=g, device="cuda") * 0.02
+    T = W + K
+    q = torch.randn((T, B, H, D), generator=g, device="cuda")
+    k = torch.randn((T, B, H, D), generator=g, device="cuda")
+    v = torch.randn((T, B, H, D), generator=g, device="cuda")
+    br = torch.randn((T, B, H), generator=g, device="cuda")
+    ar = torch.randn((T, B, H), generator=g, device="cuda")
+    A = -torch.ones(H, device="cuda")
+    dt = torch.zeros(H, device="cuda")
+    o = torch.empty((B, H, D), device="cuda")
+    for i in range(W):
+        vxg_b200.deltanet_step(ctx, q[i], k[i], v[i], br[i], ar[i], A, dt, state, o=o)
+    ctx.sync()
+    sampler = ClockSampler(local)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier(torch, dist, world)
+    sampler.start()
+    e0.record()
+    for i in range(W, T):
+        vxg_b200.deltanet_step(ctx, q[i], k[i], v[i], br[i], ar[i], A, dt, state, o=o)
+    e1.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    ms = barrier_max(torch, dist, world, e0.elapsed_time(e1))
+    alg = 2 * B * H * D * D * 4 + B * H * 4 * D * 4
+    peak, peak_kind = measured_peaks()
+    ach = alg / (ms / K * 1e-3) / 1e9
+    return {
+        "metric": "gated-DeltaNet decode step: HBM GB/s and seq-steps/s",
+        "value": B * world * K / (ms * 1e-3), "unit": "seq-steps/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config4: DeltaNet decode, 64 seqs x 32 heads, dk=dv=128, fp32 "
+                               "state N(0,0.02^2) read+written every step",
+                   "l2": "state larger than L2 (268 MB per step)"},
+        "roofline": {"kernel": "deltanet_step_kernel", "bound": "hbm", "achieved": ach,
+                     "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": peak_kind,
+                     "traffic": profile_traffic("deltanet_step_config4.json")},
+        "gpu_launches": K, "clocks": sampler.summary(),
+    }
+
+
+def run_long(args, world, rank, local):
+    """BASELINE config 3 on one GPU: B=1, ctx 262144, 1% of K rows x8, split-KV across SMs."""
+    import torch
+    import torch.distributed as dist
+    import vxg_b200
+    from vxg_b200 import workloads as wl
+    K, W = args.steps, args.warmup
+    ctx = vxg_b200.Context()
+    L = 262144
+    cap = L + W + K + 8
+    pool = vxg_b200.KvQ8Pool(ctx, 1, wl.HKV, wl.HD, cap)
+    wl.fill_pool_device(pool, [L], seed=3, outlier_frac=0.01)
+    q, kn, vn = wl.decode_step_inputs_device(1, W + K, seed=4)
+    seq = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pos = [torch.tensor([L + i], dtype=torch.int32, device="cuda") for i in range(W + K)]
+    out = torch.empty((1, wl.HQ, wl.HD), device="cuda")
+    for i in range(W):
+        pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=out, max_ctx=cap)
+    ctx.sync()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier(torch, dist, world)
+    ctx.set_timing(True)
+    e0.record()
+    for i in range(W, W + K):
+        pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=out, max_ctx=cap)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    split = ctx.split_ms_total() / K
+    alg = (L + W + K / 2) * wl.TOKEN_BYTES
+    peak, peak_kind = measured_peaks()
+    ach = alg / (split * 1e-3) / 1e9
+    return {"metric": METRIC, "value": K / (ms * 1e-3), "unit": "seq-steps/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config3: B=1 ctx 262144, 1% K rows x8, split-KV over SMs"},
+            "roofline": {"kernel": "decode_fast_split", "bound": "hbm", "achieved": ach,
+                         "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                         "peak_kind": peak_kind, "split_ms_per_launch": split},
+            "gpu_launches": 3 * K}
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args, world, rank):
+    """The reference algorithm (the C restatement of the Rust CPU operators; the Rust crate
+    cannot be built here) on this host's cores, on a bounded sample of the same workload."""
+    from oracle import oracle
+    from vxg_b200 import workloads as wl
+    K, W = args.steps, args.warmup
+    cores = host_cores()
+    batch = wl.DecodeBatch(seed=1)
+    lens = batch.ctx_lens()
+    S = int(min(batch.n_seq, max(4, cores)))
+    lens = lens[:S]
+    rng = np.random.default_rng(17)
+    cap = int(lens.max()) + W + K + 1
+    nb = wl.HD // 32
+    kpool = np.zeros((S, cap, wl.HKV, nb, 34), np.uint8)
+    vpool = np.zeros_like(kpool)
+    for s in range(S):
+        for t0 in range(0, int(lens[s]), 4096):
+            n = min(4096, int(lens[s]) - t0)
+            kpool[s, t0:t0 + n] = oracle.q8_quantize(
+                rng.standard_normal((n, wl.HKV, wl.HD), dtype=np.float32))
+            vpool[s, t0:t0 + n] = oracle.q8_quantize(
+                rng.standard_normal((n, wl.HKV, wl.HD), dtype=np.float32))
+    kflat, vflat = kpool.reshape(-1), vpool.reshape(-1)
+    seq = np.arange(S, dtype=np.int32)
+
+    def step(i):
+        q = rng.standard_normal((S, wl.HQ, wl.HD), dtype=np.float32)
+        kn = rng.standard_normal((S, wl.HKV, wl.HD), dtype=np.float32)
+        vn = rng.standard_normal((S, wl.HKV, wl.HD), dtype=np.float32)
+        t = time.perf_counter()
+        oracle.batch_decode_q8(seq, (lens + i).astype(np.int32), q, kn, vn, kflat, vflat, cap,
+                               wl.HQ, wl.HKV, wl.HD, do_append=True, n_threads=cores)
+        return time.perf_counter() - t
+
+    for i in range(W):
+        step(i)
+    el = sum(step(W + i) for i in range(K))
+    v = S * K / el
+    sample = (f"{S} of the 64 config-2 sequences (mean ctx {lens.mean():.0f}) per step, one "
+              f"append+attend each, {cores} threads")
+    return {"metric": METRIC, "value": v, "unit": "seq-steps/s", "impl": "reference",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": el / K * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "config2: batched decode + Q8 append, 64 seqs per GPU, ctx "
+                                   "U[1024,32768], 16 q / 2 kv heads, head_dim 256, Q8_0 KV "
+                                   "(34-B blocks)", "seqs_per_step_sampled": S},
+            "cpu_baseline": {"value": v, "unit": "seq-steps/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "seq-steps/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "long", "deltanet"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args, world, rank)), flush=True)
+        return
+    import torch
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    try:
+        fn = {"decode": run_decode, "deltanet": run_deltanet, "long": run_long}[args.workload]
+        res = fn(args, world, rank, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

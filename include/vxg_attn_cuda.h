@@ -1,0 +1,178 @@
+/*
+ * vxg_attn_cuda.h -- C ABI of the B200 (sm_100a) backend for the vxg-tensor attention hot path:
+ * Q8_0 KV-cache append, split-KV GQA decode attention over that cache, and the gated-DeltaNet
+ * recurrent state update.
+ *
+ * It extends the reference's native GPU ABI conventions (native/abi.h:1-10, native/cuda.cu:31-68):
+ *   - create() returns an opaque handle or NULL and writes a message into (err, cap);
+ *   - every other call returns int: 0 = ok, < 0 = error class (values of include/vxg.h:22-30),
+ *     and writes a message into (err, cap) on failure;
+ *   - a failed call synchronises its stream before returning, so no copy still targets caller
+ *     memory (native/cuda.cu:62-65);
+ *   - a device (CUDA) error poisons the context: every later call fails with
+ *     VXG_ATTN_ERR_INTERNAL, like a failed GPU state in the reference (docs/GPU.md:5-8,
+ *     crates/vxg-tensor/src/llm.rs:546-550).  There is no CPU fallback.
+ * Plain C types only: pointers, sizes, ints, floats.
+ *
+ * KV layout (unchanged from the reference): a KV pool holds, for each of n_seq sequences, cap
+ * tokens of KvQ8Block[n_head_kv][head_dim/32] for K and the same for V, i.e. the byte image of
+ * the reference's per-layer Vec<KvQ8Block> (crates/vxg-tensor/src/llm_prefill.rs:17-24,
+ * 311-324) at offset seq * cap * n_head_kv * (head_dim/32) * 34.
+ *
+ * Pointers marked "mem" are host or device memory according to the call's `memkind`.  With
+ * VXG_ATTN_MEM_HOST the call copies in and out itself (pinned host memory is fastest; see
+ * vxg_attn_cuda_host_alloc).  `stream` may be NULL: the call then runs on the context's stream
+ * and returns when the results are in place.  A non-NULL stream (cudaStream_t) makes
+ * device-memory calls asynchronous on that stream; call vxg_attn_cuda_sync to collect device
+ * status.  One context per host thread; contexts are not thread-safe.
+ */
+#ifndef VXG_ATTN_CUDA_H
+#define VXG_ATTN_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VXG_ATTN_API __attribute__((visibility("default")))
+#else
+#define VXG_ATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (values of the reference's include/vxg.h:22-30). */
+#define VXG_ATTN_OK 0
+#define VXG_ATTN_WARN_NONFINITE 1       /* success, but an output is NaN/Inf (as on the CPU)   */
+#define VXG_ATTN_ERR_NULL_PTR (-1)
+#define VXG_ATTN_ERR_INVALID_OPTION (-2)
+#define VXG_ATTN_ERR_BUFFER_TOO_SMALL (-3)
+#define VXG_ATTN_ERR_UNSUPPORTED (-6)
+#define VXG_ATTN_ERR_INTERNAL (-7)      /* CUDA error; the context is poisoned                 */
+
+#define VXG_ATTN_MEM_HOST 0
+#define VXG_ATTN_MEM_DEVICE 1
+
+/* Library version string. */
+VXG_ATTN_API const char* vxg_attn_cuda_version(void);
+
+/* ---------------------------------------------------------------- context ------------------ */
+/* Binds device $VXG_CUDA_DEVICE (default: the current device), creates a stream; on success
+ * writes the device name into err.  Mirrors vxg_cuda_create (native/cuda.cu:31-41). */
+VXG_ATTN_API void* vxg_attn_cuda_create(char* err, size_t cap);
+/* Synchronises and frees the context (native/cuda.cu:68). */
+VXG_ATTN_API void vxg_attn_cuda_destroy(void* ctx);
+/* Waits for all work on `stream` (NULL: the context stream), then reports the device status
+ * word: VXG_ATTN_WARN_NONFINITE, VXG_ATTN_ERR_INVALID_OPTION for skipped out-of-range entries,
+ * VXG_ATTN_ERR_INTERNAL for a device error or a bounded wait that gave up. */
+VXG_ATTN_API int vxg_attn_cuda_sync(void* ctx, void* stream, char* err, size_t cap);
+/* Number of SMs of the bound device (the split-KV grid size). */
+VXG_ATTN_API int vxg_attn_cuda_sm_count(void* ctx);
+/* Device time in ms of the last split-KV attention pass launched on the context (when timing
+ * is enabled with vxg_attn_cuda_set_timing); -1 if unavailable.  Like the reference's
+ * kernel_ms out-parameter (native/cuda.cu:52-60). */
+VXG_ATTN_API int vxg_attn_cuda_set_timing(void* ctx, int enable);
+VXG_ATTN_API double vxg_attn_cuda_last_split_ms(void* ctx);
+/* Test hook: 1 forces the portable split kernel for every shape (cross-check of the fast one). */
+VXG_ATTN_API int vxg_attn_cuda_force_generic(void* ctx, int enable);
+
+/* Device / pinned memory for callers without a CUDA toolchain (Rust, C). */
+VXG_ATTN_API void* vxg_attn_cuda_malloc(void* ctx, size_t bytes, char* err, size_t cap);
+VXG_ATTN_API void vxg_attn_cuda_free(void* ctx, void* dptr);
+VXG_ATTN_API void* vxg_attn_cuda_host_alloc(void* ctx, size_t bytes, char* err, size_t cap);
+VXG_ATTN_API void vxg_attn_cuda_host_free(void* ctx, void* hptr);
+/* kind: 0 host->device, 1 device->host, 2 device->device.  Synchronous. */
+VXG_ATTN_API int vxg_attn_cuda_memcpy(void* ctx, void* dst, const void* src, size_t bytes, int kind, char* err,
+                         size_t cap);
+
+/* ---------------------------------------------------------------- Q8 KV pool --------------- */
+/* Replaces the per-layer Vec<KvQ8Block> pair of LlmState (crates/vxg-tensor/src/llm.rs:36-41,
+ * 290-338) and vxt_metal_cb4_fast_state_create (crates/vxg-tensor/src/metal_cb4_fast_ffi.rs:
+ * 149-154): zero-filled device K and V pools of n_seq x cap_tokens tokens.  head_dim must be a
+ * multiple of 32 (llm.rs:291). */
+VXG_ATTN_API void* vxg_attn_cuda_kv_create(void* ctx, uint32_t n_seq, uint32_t n_head_kv, uint32_t head_dim,
+                              uint32_t cap_tokens, char* err, size_t cap);
+VXG_ATTN_API void vxg_attn_cuda_kv_destroy(void* kv);
+/* Bytes held by the K and V pools (metal_cb4_fast_ffi.rs:157, llm.rs:340-346). */
+VXG_ATTN_API size_t vxg_attn_cuda_kv_bytes(void* kv);
+VXG_ATTN_API uint32_t vxg_attn_cuda_kv_capacity(void* kv);
+/* Grows every sequence to at least cap_tokens tokens, keeping contents (doubling policy of
+ * native/metal_cb4_fast.h:174-191). */
+VXG_ATTN_API int vxg_attn_cuda_kv_reserve(void* kv, uint32_t cap_tokens, char* err, size_t cap);
+/* Device base pointers of the K and V pools and the byte stride between sequences. */
+VXG_ATTN_API int vxg_attn_cuda_kv_device_ptrs(void* kv, void** k_pool, void** v_pool, size_t* seq_stride);
+/* Byte-identical import / export of tokens [tok_begin, tok_begin + n_tok) of sequence `seq`:
+ * k_blocks / v_blocks are n_tok * n_head_kv * head_dim/32 KvQ8Blocks (34 B each), i.e. a slice
+ * of the reference's Vec<KvQ8Block>. */
+VXG_ATTN_API int vxg_attn_cuda_kv_import(void* ctx, void* kv, uint32_t seq, uint32_t tok_begin, uint32_t n_tok,
+                            const void* k_blocks, const void* v_blocks, int memkind, char* err,
+                            size_t cap);
+VXG_ATTN_API int vxg_attn_cuda_kv_export(void* ctx, void* kv, uint32_t seq, uint32_t tok_begin, uint32_t n_tok,
+                            void* k_blocks, void* v_blocks, int memkind, char* err, size_t cap);
+
+/* ---------------------------------------------------------------- ops ---------------------- */
+/* Quantise-and-append (llm_prefill.rs:311-324 with KvQ8Block::quantize, :27-42), bit-exact:
+ * for b < n_batch, t < n_tok: k_new/v_new[b][t][n_head_kv][head_dim] (f32, mem) go to sequence
+ * seq_ids[b] at position pos[b] + t.  seq_ids, pos: int32 [n_batch] (mem). */
+VXG_ATTN_API int vxg_attn_cuda_q8_append(void* ctx, void* kv, uint32_t n_batch, uint32_t n_tok,
+                            const int32_t* seq_ids, const int32_t* pos, const float* k_new,
+                            const float* v_new, int memkind, void* stream, char* err, size_t cap);
+
+/* Batched decode step = append then attend, the order of step_full_gqa_q8
+ * (llm_prefill.rs:311-369): for each b, if k_new != NULL the new token's K/V
+ * ([n_batch][n_head_kv][head_dim] f32) is appended at pos[b] of seq_ids[b]; then the query
+ * q[b] ([n_head][head_dim] f32, already normed / RoPE'd) attends to tokens [0, pos[b]] with
+ * softmax scale `scale` (1/sqrt(head_dim) in the reference).  q_gate (nullable, same shape as q)
+ * applies out *= sigmoid(gate) (llm_prefill.rs:363-368).  out: [n_batch][n_head][head_dim].
+ * max_ctx: an upper bound of pos[b] + 1 (0 = the pool capacity). */
+VXG_ATTN_API int vxg_attn_cuda_q8_decode(void* ctx, void* kv, uint32_t n_batch, uint32_t n_head,
+                            const int32_t* seq_ids, const int32_t* pos, const float* q,
+                            const float* k_new, const float* v_new, const float* q_gate,
+                            float scale, uint32_t max_ctx, float* out, int memkind, void* stream,
+                            char* err, size_t cap);
+
+/* Split-KV partial over tokens [kv_begin[b], kv_end[b]) of each sequence (no append): per
+ * (b, head) the running max m (log2 units: max_t score_t * log2(e)), the sum
+ * l = sum_t 2^(score_t*log2(e) - m) and the unnormalised o = sum_t 2^(...) * v_t.  Shapes:
+ * m, l [n_batch][n_head]; o [n_batch][n_head][head_dim].  Empty ranges give m = -inf, l = 0,
+ * o = 0.  This is the per-GPU half of the multi-GPU KV-range split. */
+VXG_ATTN_API int vxg_attn_cuda_q8_decode_partial(void* ctx, void* kv, uint32_t n_batch, uint32_t n_head,
+                                    const int32_t* seq_ids, const int32_t* kv_begin,
+                                    const int32_t* kv_end, const float* q, float scale,
+                                    uint32_t max_ctx, float* m, float* l, float* o, int memkind,
+                                    void* stream, char* err, size_t cap);
+
+/* Log-sum-exp merge of n_parts partials (layout [n_parts][n_rows] for m and l,
+ * [n_parts][n_rows][head_dim] for o) into out [n_rows][head_dim]; optional sigmoid gate. */
+VXG_ATTN_API int vxg_attn_cuda_lse_combine(void* ctx, uint32_t n_parts, uint32_t n_rows, uint32_t head_dim,
+                              const float* m, const float* l, const float* o, const float* gate,
+                              float* out, int memkind, void* stream, char* err, size_t cap);
+
+/* Drop-in for step_full_gqa_q8 (llm_prefill.rs:259-278) on host buffers for one sequence `seq`
+ * of `kv`: q_raw [n_head][hd] (or [n_head][2*hd] with gated_q), k_cur (updated in place with
+ * the normed / RoPE'd K, as in the reference), v_cur [n_head_kv][hd], optional q_norm/k_norm
+ * [hd] RMSNorm weights, RoPE parameters, appends at `pos` and writes attn_out [n_head][hd]. */
+VXG_ATTN_API int vxg_attn_cuda_step_full_gqa_q8(void* ctx, void* kv, uint32_t seq, const float* q_raw,
+                                   float* k_cur, const float* v_cur, const float* q_norm,
+                                   const float* k_norm, int gated_q, uint32_t n_head,
+                                   uint32_t n_head_kv, uint32_t head_dim, uint32_t pos,
+                                   uint32_t rope_pos, uint32_t rope_dim, float rope_freq_base,
+                                   int rope_neox, float eps, float* attn_out, char* err,
+                                   size_t cap);
+
+/* Gated-DeltaNet core step (llm_ops.rs:139-184) for n_batch sequences:
+ * q, k [n_batch][n_kh][dk] (raw, L2-normalised inside, q also scaled by q_scale, 1/sqrt(dk) in
+ * the reference), v [n_batch][n_vh][dv], beta_raw / alpha_raw [n_batch][n_vh], ssm_a / dt_bias
+ * [n_vh]; state [n_batch][n_vh][dv][dk] updated in place; o [n_batch][n_vh][dv] = S_new q.
+ * dk in {64, 128, 256}; dv a multiple of 32. */
+VXG_ATTN_API int vxg_attn_cuda_deltanet_step(void* ctx, uint32_t n_batch, uint32_t n_kh, uint32_t n_vh,
+                                uint32_t dk, uint32_t dv, const float* q, const float* k,
+                                const float* v, const float* beta_raw, const float* alpha_raw,
+                                const float* ssm_a, const float* dt_bias, float q_scale, float eps,
+                                float* state, float* o, int memkind, void* stream, char* err,
+                                size_t cap);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VXG_ATTN_CUDA_H */

@@ -1,0 +1,791 @@
+// Split-KV GQA decode attention over the Q8_0 KV cache, plus the log-sum-exp combine.
+//
+// Reference semantics: the attention half of step_full_gqa_q8
+// (crates/vxg-tensor/src/llm_prefill.rs:326-369): for each query head h (kv head h / (n_head /
+// n_kv)), s_t = scale * sum_b d_b * sum_i code_i q_i (KvQ8Block::dot_f32, :45-54), softmax over
+// t in [0, seq_len), out = sum_t p_t * d_b * code (KvQ8Block::axpy_f32, :57-62), optional
+// sigmoid gate (:363-368).  Results agree with the reference to fp32-accumulation tolerance,
+// not bit for bit (the reference sums tokens in order; here tokens are split across SMs and
+// merged with an exact log-sum-exp rescale).
+//
+// Two split kernels feed one combine kernel:
+//  * decode_fast_split  -- head_dim 256, 8 query heads per kv head, 2 kv heads (the Qwen3.5
+//    full-attention shape).  Persistent: one CTA per SM takes an equal share of all
+//    64-token units of the batch, so ragged contexts load-balance to within one unit.  Raw
+//    34-byte blocks are staged with 1-D bulk async copies (3-deep ring, mbarrier completion),
+//    QK^T runs on int8 tensor cores (m16n8k32; the q vector is split into two int8 digits,
+//    the K codes feed the MMA unchanged), PV runs on f16 tensor cores (m16n8k16; codes
+//    widened exactly to f16, the per-token V scale folded into P).
+//  * decode_generic_split -- any n_head / n_kv / head_dim (multiple of 32): FFMA, one warp per
+//    token, warp reductions.  Used for every other shape and as a cross-check.
+#include "kernels.h"
+
+#include <algorithm>
+
+namespace vxg {
+
+namespace {
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kGenChunk = 512;  // tokens per split in the generic kernel
+}
+
+// =============================================================================================
+// Generic split kernel
+// =============================================================================================
+template <int NB, int HPC>
+__global__ void __launch_bounds__(128) decode_generic_split(DecodeArgs a, Partials part,
+                                                            int max_split) {
+  constexpr int HD = NB * 32;
+  __shared__ float sm_m[4][HPC], sm_l[4][HPC];
+  __shared__ float sm_o[4][HPC][HD];
+  const int j = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = a.n_head / a.n_kv;
+  const int h0 = hg * HPC;        // first query head of this CTA
+  const int kh = h0 / G;          // its kv head
+  const int s = a.seq_ids[b];
+  const int beg = a.kv_begin ? a.kv_begin[b] : 0;
+  const int end = a.kv_end[b] + a.end_add;
+  if (s < 0 || s >= a.n_seq || beg < 0 || end > a.cap || beg > end) return;
+  if (beg + j * kGenChunk >= end) return;
+  const int per_tok = a.n_kv * NB;
+  const size_t seq_base = (size_t)s * a.cap * per_tok;
+  const uint8_t* kb = a.k_pool + (seq_base + (size_t)kh * NB) * kBlk;
+  const uint8_t* vb = a.v_pool + (seq_base + (size_t)kh * NB) * kBlk;
+
+  float qv[HPC][NB];
+#pragma unroll
+  for (int g = 0; g < HPC; ++g)
+#pragma unroll
+    for (int c = 0; c < NB; ++c)
+      qv[g][c] = a.q[((size_t)b * a.n_head + h0 + g) * HD + c * 32 + lane] * (a.scale * kLog2e);
+  float m[HPC], l[HPC], o[HPC][NB];
+#pragma unroll
+  for (int g = 0; g < HPC; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int c = 0; c < NB; ++c) o[g][c] = 0.f;
+  }
+  // chunks j, j + gridDim.x, ... of this entry all fold into this CTA's running state
+  for (int t0 = beg + j * kGenChunk; t0 < end; t0 += gridDim.x * kGenChunk)
+  for (int t = t0 + warp, t1 = min(end, t0 + kGenChunk); t < t1; t += 4) {
+    const uint8_t* kr = kb + (size_t)t * per_tok * kBlk;
+    const uint8_t* vr = vb + (size_t)t * per_tok * kBlk;
+    float kx[NB], vx[NB];
+#pragma unroll
+    for (int c = 0; c < NB; ++c) {
+      const float kd = f16bits_to_f32(*reinterpret_cast<const uint16_t*>(kr + c * kBlk));
+      const float vd = f16bits_to_f32(*reinterpret_cast<const uint16_t*>(vr + c * kBlk));
+      kx[c] = (float)(int8_t)kr[c * kBlk + 2 + lane] * kd;
+      vx[c] = (float)(int8_t)vr[c * kBlk + 2 + lane] * vd;
+    }
+#pragma unroll
+    for (int g = 0; g < HPC; ++g) {
+      float acc = 0.f;
+#pragma unroll
+      for (int c = 0; c < NB; ++c) acc = fmaf(kx[c], qv[g][c], acc);
+      const float sg = warp_sum(acc);
+      // a NaN score (non-finite query) must reach the output as NaN, as on the CPU: keep the
+      // running max finite so the log-sum-exp merge does not drop this partial.
+      const float mn = sg == sg ? fmaxf(m[g], sg) : (m[g] == -INFINITY ? 0.f : m[g]);
+      const float alpha = exp2f(m[g] - mn);
+      const float p = exp2f(sg - mn);
+      l[g] = l[g] * alpha + p;
+      m[g] = mn;
+#pragma unroll
+      for (int c = 0; c < NB; ++c) o[g][c] = fmaf(p, vx[c], o[g][c] * alpha);
+    }
+  }
+  if (lane == 0)
+#pragma unroll
+    for (int g = 0; g < HPC; ++g) {
+      sm_m[warp][g] = m[g];
+      sm_l[warp][g] = l[g];
+    }
+#pragma unroll
+  for (int g = 0; g < HPC; ++g)
+#pragma unroll
+    for (int c = 0; c < NB; ++c) sm_o[warp][g][c * 32 + lane] = o[g][c];
+  __syncthreads();
+  const size_t slot = (size_t)b * max_split + j;
+  for (int idx = threadIdx.x; idx < HPC * HD; idx += blockDim.x) {
+    const int g = idx / HD, d = idx - g * HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w][g]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float f = sm_m[w][g] == -INFINITY ? 0.f : exp2f(sm_m[w][g] - M);
+      L = fmaf(sm_l[w][g], f, L);
+      O = fmaf(sm_o[w][g][d], f, O);
+    }
+    part.o[(slot * a.n_head + h0 + g) * HD + d] = O;
+    if (d == 0) {
+      part.m[slot * a.n_head + h0 + g] = M;
+      part.l[slot * a.n_head + h0 + g] = L;
+    }
+  }
+}
+
+// =============================================================================================
+// Fast split kernel (head_dim 256, GQA group 8, 2 kv heads)
+// =============================================================================================
+namespace fast {
+constexpr int NB = 8;              // 32-dim blocks per head
+constexpr int HD = 256;
+constexpr int G = 8;               // query heads per kv head
+constexpr int NKV = 2;             // kv heads (both handled by every CTA)
+constexpr int REC = NB * kBlk;     // 272 B per (token, kv head)
+constexpr int TOKB = NKV * REC;    // 544 B per token in one cache
+constexpr int ST = 64;             // tokens per unit / stage
+constexpr int NS = 3;              // stages in flight
+constexpr int STB = ST * TOKB;     // 34816 B per stage per cache
+constexpr int THREADS = 256;       // 8 warps = 2 kv heads x 4 sub-tiles of 16 tokens
+constexpr int SROW = ST + 2;       // scale row stride (floats): conflict-free, 8-B aligned
+constexpr int MAXB = 1024;         // batch entries per launch
+constexpr uint32_t kWaitIters = 1u << 26;
+
+struct __align__(128) Smem {
+  uint8_t stage[NS][2][STB];       // [buf][K, V][token][kv head][block] raw KvQ8Blocks
+  float sk[NKV * NB][SROW];        // K scales of the current stage, [kv head * 8 + block][token]
+  float sv[NKV * NB][SROW];        // V scales
+  float mrg_m[8][G];
+  float mrg_l[8][G];
+  long long prefix[MAXB + 1];      // units before batch entry b
+  uint64_t full[NS];
+};
+}  // namespace fast
+
+size_t fast_smem_bytes() { return sizeof(fast::Smem); }
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) {
+  return *reinterpret_cast<const uint32_t*>(p);
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// Four codes of one 32-code block as an aligned 32-bit word.  The 34-byte blocks sit at byte
+// 34*c of a 16-byte aligned 272-byte record, so odd blocks have their codes 4-byte aligned and
+// even blocks are offset by 2.  Each block is cut into 8 "groups" of 4 codes that can be read
+// as whole words:
+//   odd c : group r = codes 4r .. 4r+3
+//   even c: group r (r >= 1) = codes 4r-2 .. 4r+1; group 0 = codes {0, 1, 30, 31}
+// The MMA reduction order inside a block is free, so queries are permuted the same way.
+template <int C>
+__device__ __forceinline__ uint32_t load_group(const uint8_t* blk, int r) {
+  if (C & 1) return lds32(blk + 2 + 4 * r);
+  uint32_t w = lds32(blk + 4 * r);
+  if (r == 0) w = prmt(w, lds32(blk + 32), 0x5432);
+  return w;
+}
+// Dimension (within the head) of byte i of group r of block c.
+__device__ __forceinline__ int group_dim(int c, int r, int i) {
+  if (c & 1) return 32 * c + 4 * r + i;
+  if (r > 0) return 32 * c + 4 * r - 2 + i;
+  return 32 * c + (i < 2 ? i : 28 + i);
+}
+
+__device__ __forceinline__ void imma_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                           uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%13};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0),
+        "r"(0));
+}
+__device__ __forceinline__ void hmma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                           uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// f16x2 holding two int8 codes exactly: bytes (x ^ 0x80) placed under the 0x64 exponent give
+// 1024 + x + 128, minus 1152.
+__device__ __forceinline__ uint32_t codes_to_f16x2(uint32_t pair_bytes, uint32_t sel) {
+  const uint32_t h = prmt(pair_bytes, 0x64646464u, sel);
+  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __halves2half2(
+                                                                       __ushort_as_half(0x6480),
+                                                                       __ushort_as_half(0x6480)));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+struct UnitInfo {
+  int b;             // batch entry
+  int t_start;       // first token
+  int ntok;          // tokens in this unit (1..64)
+  int s;             // sequence id
+};
+
+__device__ __forceinline__ int find_batch(const long long* prefix, int B, long long u) {
+  int lo = 0, hi = B - 1;  // largest b with prefix[b] <= u
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= u) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ UnitInfo unit_info(const DecodeArgs& a, const long long* prefix,
+                                              long long u) {
+  UnitInfo r;
+  r.b = find_batch(prefix, a.n_batch, u);
+  const int beg = a.kv_begin ? a.kv_begin[r.b] : 0;
+  const int end = a.kv_end[r.b] + a.end_add;
+  r.t_start = beg + (int)(u - prefix[r.b]) * fast::ST;
+  r.ntok = min(fast::ST, end - r.t_start);
+  r.s = a.seq_ids[r.b];
+  return r;
+}
+
+__device__ __forceinline__ bool entry_valid(const DecodeArgs& a, int b) {
+  const int s = a.seq_ids[b];
+  const int beg = a.kv_begin ? a.kv_begin[b] : 0;
+  const int end = a.kv_end[b] + a.end_add;
+  return !(s < 0 || s >= a.n_seq || beg < 0 || end > a.cap || beg > end);
+}
+// Validated length of batch entry b (0 for invalid entries, which get no units).
+__device__ __forceinline__ int entry_len(const DecodeArgs& a, int b) {
+  if (!entry_valid(a, b)) return 0;
+  return a.kv_end[b] + a.end_add - (a.kv_begin ? a.kv_begin[b] : 0);
+}
+
+__global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs a,
+                                                                       Partials part) {
+  using namespace fast;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int kh = warp & 1, sub = warp >> 1;
+  const int B = a.n_batch;
+
+  // ---- unit prefix over the batch (warp 0: serial per lane chunk + warp scan) -----------
+  if (warp == 0) {
+    const int per = (B + 31) / 32;
+    long long run = 0;
+    for (int i = 0; i < per; ++i) {
+      const int bb = lane * per + i;
+      if (bb < B) run += (entry_len(a, bb) + ST - 1) / ST;
+    }
+    long long incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    long long acc = incl - run;
+    for (int i = 0; i < per; ++i) {
+      const int bb = lane * per + i;
+      if (bb < B) {
+        sm.prefix[bb] = acc;
+        acc += (entry_len(a, bb) + ST - 1) / ST;
+      }
+    }
+    if (lane == 31) sm.prefix[B] = incl;
+  }
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) mbar_init(&sm.full[i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const long long U = sm.prefix[B];
+  const long long u0 = (long long)blockIdx.x * U / gridDim.x;
+  const long long u1 = (long long)(blockIdx.x + 1) * U / gridDim.x;
+  if (u0 >= u1) return;
+
+  auto issue = [&](long long u, int buf) {
+    const UnitInfo ui = unit_info(a, sm.prefix, u);
+    const uint32_t bytes = (uint32_t)ui.ntok * TOKB;
+    const size_t off = ((size_t)ui.s * a.cap + ui.t_start) * TOKB;
+    mbar_arrive_expect_tx(&sm.full[buf], 2 * bytes);
+    bulk_g2s(sm.stage[buf][0], a.k_pool + off, bytes, &sm.full[buf]);
+    bulk_g2s(sm.stage[buf][1], a.v_pool + off, bytes, &sm.full[buf]);
+  };
+  if (tid == 0)
+    for (int i = 0; i < NS && u0 + i < u1; ++i) issue(u0 + i, i);
+
+  uint32_t qa[NB][4];      // int8 digit fragments of this warp's 8 query heads
+  float fac = 0.f;         // per-head factor sigma/254 * scale * log2(e) (head g)
+  float o[NB][2][4];       // O^T accumulators: [block][m-tile][frag]
+  float m_run = -INFINITY, l_run = 0.f;
+  int cur_b = -1;
+
+  for (long long u = u0; u < u1; ++u) {
+    const int it = (int)(u - u0);
+    const int buf = it % NS;
+    const uint32_t par = (uint32_t)(it / NS) & 1u;
+    const UnitInfo ui = unit_info(a, sm.prefix, u);
+
+    if (ui.b != cur_b) {
+      // ---- query digits: q ~= sigma * (d_a + d_b / 254), sigma = max|q| / 127 ------------
+      cur_b = ui.b;
+      const float* qh = a.q + ((size_t)ui.b * a.n_head + kh * G + g) * HD;
+      float amax = 0.f;
+      bool nonfinite = false;
+#pragma unroll
+      for (int c = 0; c < NB; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float x = qh[group_dim(c, 2 * q + (i >> 2), i & 3)];
+          amax = fmaxf(amax, fabsf(x));
+          nonfinite |= !isfinite(x);
+        }
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, 1) != 0;
+      nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, 2) != 0;
+      const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+#pragma unroll
+      for (int c = 0; c < NB; ++c) {
+        uint32_t da[2] = {0, 0}, db[2] = {0, 0};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float z = qh[group_dim(c, 2 * q + (i >> 2), i & 3)] * inv;
+          float ra = rintf(z);
+          ra = fminf(fmaxf(ra, -127.f), 127.f);
+          float rb = rintf((z - ra) * 254.0f);
+          rb = fminf(fmaxf(rb, -127.f), 127.f);
+          const int ia = (ra == ra) ? (int)ra : 0;
+          const int ib = (rb == rb) ? (int)rb : 0;
+          da[i >> 2] |= ((uint32_t)ia & 0xffu) << (8 * (i & 3));
+          db[i >> 2] |= ((uint32_t)ib & 0xffu) << (8 * (i & 3));
+        }
+        qa[c][0] = da[0];  // rows 0-7 (digit a), k 4q..4q+3   = group 2q
+        qa[c][1] = db[0];  // rows 8-15 (digit b), same k
+        qa[c][2] = da[1];  // rows 0-7, k 16+4q..               = group 2q+1
+        qa[c][3] = db[1];
+      }
+      fac = (amax / 127.0f) * (1.0f / 254.0f) * a.scale * kLog2e;
+      if (nonfinite) fac = __int_as_float(0x7fffffff);  // NaN: the head's output becomes NaN
+      m_run = -INFINITY;
+      l_run = 0.f;
+#pragma unroll
+      for (int c = 0; c < NB; ++c)
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[c][mt][e] = 0.f;
+    }
+
+    // ---- wait for this stage (bounded) ----------------------------------------------------
+    const bool ok = __syncthreads_and(mbar_wait(&sm.full[buf], par, kWaitIters));
+    if (!ok) {
+      // Give up: flag it, let the copies this CTA issued land (bounded), then leave.
+      if (tid == 0) atomicOr(a.status, kStatusTimeout);
+      for (int k = 1; k < NS; ++k)
+        if (u + k < u1) mbar_wait(&sm.full[(it + k) % NS], (uint32_t)((it + k) / NS) & 1u, kWaitIters);
+      return;
+    }
+    const uint8_t* kst = sm.stage[buf][0];
+    const uint8_t* vst = sm.stage[buf][1];
+
+    // ---- scales of the stage to f32 (0 for tokens past the unit) ---------------------------
+#pragma unroll
+    for (int r = 0; r < (2 * NKV * NB * ST) / THREADS; ++r) {
+      const int e = tid + r * THREADS;
+      const int c = e & 7, hh = (e >> 3) & 1, t = (e >> 4) & (ST - 1), which = e >> 10;
+      const uint8_t* base = (which ? vst : kst) + t * TOKB + hh * REC + c * kBlk;
+      const float d = t < ui.ntok ? f16bits_to_f32(*reinterpret_cast<const uint16_t*>(base)) : 0.f;
+      (which ? sm.sv : sm.sk)[hh * NB + c][t] = d;
+    }
+    __syncthreads();
+
+    if (16 * sub < ui.ntok) {
+      // ---- S = Q K^T on int8 tensor cores: 2 n-tiles of 8 tokens -----------------------------
+      float sacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint8_t* rec = kst + (16 * sub + 8 * j + g) * TOKB + kh * REC;
+#pragma unroll
+        for (int c = 0; c < NB; ++c) {
+          uint32_t b0, b1;
+          switch (c) {
+            case 0: b0 = load_group<0>(rec, 2 * q); b1 = load_group<0>(rec, 2 * q + 1); break;
+            case 1: b0 = load_group<1>(rec + 1 * kBlk, 2 * q); b1 = load_group<1>(rec + 1 * kBlk, 2 * q + 1); break;
+            case 2: b0 = load_group<0>(rec + 2 * kBlk, 2 * q); b1 = load_group<0>(rec + 2 * kBlk, 2 * q + 1); break;
+            case 3: b0 = load_group<1>(rec + 3 * kBlk, 2 * q); b1 = load_group<1>(rec + 3 * kBlk, 2 * q + 1); break;
+            case 4: b0 = load_group<0>(rec + 4 * kBlk, 2 * q); b1 = load_group<0>(rec + 4 * kBlk, 2 * q + 1); break;
+            case 5: b0 = load_group<1>(rec + 5 * kBlk, 2 * q); b1 = load_group<1>(rec + 5 * kBlk, 2 * q + 1); break;
+            case 6: b0 = load_group<0>(rec + 6 * kBlk, 2 * q); b1 = load_group<0>(rec + 6 * kBlk, 2 * q + 1); break;
+            default: b0 = load_group<1>(rec + 7 * kBlk, 2 * q); b1 = load_group<1>(rec + 7 * kBlk, 2 * q + 1); break;
+          }
+          int acc[4];
+          imma_16832(acc, qa[c], b0, b1);
+          const int x0 = 254 * acc[0] + acc[2];
+          const int x1 = 254 * acc[1] + acc[3];
+          const float2 d = *reinterpret_cast<const float2*>(&sm.sk[kh * NB + c][16 * sub + 8 * j + 2 * q]);
+          sacc[j][0] = fmaf(d.x, __int2float_rn(x0), sacc[j][0]);
+          sacc[j][1] = fmaf(d.y, __int2float_rn(x1), sacc[j][1]);
+        }
+      }
+      // ---- online softmax (log2 domain) ----------------------------------------------------
+      float p[2][2];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tl = 16 * sub + 8 * j + 2 * q + e;
+          p[j][e] = tl < ui.ntok ? sacc[j][e] * fac : -INFINITY;
+          mx = fmaxf(mx, p[j][e]);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      if (fac != fac) mx = 0.f;  // keep the running max finite so the NaN survives the merge
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = exp2f(m_run - m_use);
+      float ps = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          p[j][e] = exp2f(p[j][e] - m_use);
+          ps += p[j][e];
+        }
+      l_run = fmaf(l_run, alpha, ps);
+      m_run = m_new;
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * q);
+        const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * q + 4);
+#pragma unroll
+        for (int c = 0; c < NB; ++c)
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            o[c][mt][0] *= a0;
+            o[c][mt][1] *= a1;
+            o[c][mt][2] *= a0;
+            o[c][mt][3] *= a1;
+          }
+      }
+      // ---- O^T += V^T P'^T on f16 tensor cores, P' = p * d_v ---------------------------------
+      const uint8_t* vrec = vst + (16 * sub + 2 * q) * TOKB + kh * REC;
+#pragma unroll
+      for (int c = 0; c < NB; ++c) {
+        const float2 dv0 = *reinterpret_cast<const float2*>(&sm.sv[kh * NB + c][16 * sub + 2 * q]);
+        const float2 dv8 = *reinterpret_cast<const float2*>(&sm.sv[kh * NB + c][16 * sub + 8 + 2 * q]);
+        const uint32_t pb0 = pack_f16x2(p[0][0] * dv0.x, p[0][1] * dv0.y);
+        const uint32_t pb1 = pack_f16x2(p[1][0] * dv8.x, p[1][1] * dv8.y);
+        const uint8_t* bp = vrec + c * kBlk;
+        uint32_t w0, w1, w8, w9;
+        if (c & 1) {
+          w0 = load_group<1>(bp, g);
+          w1 = load_group<1>(bp + TOKB, g);
+          w8 = load_group<1>(bp + 8 * TOKB, g);
+          w9 = load_group<1>(bp + 9 * TOKB, g);
+        } else {
+          w0 = load_group<0>(bp, g);
+          w1 = load_group<0>(bp + TOKB, g);
+          w8 = load_group<0>(bp + 8 * TOKB, g);
+          w9 = load_group<0>(bp + 9 * TOKB, g);
+        }
+        w0 ^= 0x80808080u;
+        w1 ^= 0x80808080u;
+        w8 ^= 0x80808080u;
+        w9 ^= 0x80808080u;
+        const uint32_t lo01 = prmt(w0, w1, 0x5140), lo23 = prmt(w0, w1, 0x7362);
+        const uint32_t hi01 = prmt(w8, w9, 0x5140), hi23 = prmt(w8, w9, 0x7362);
+        hmma_16816(o[c][0], codes_to_f16x2(lo01, 0x4140), codes_to_f16x2(lo01, 0x4342),
+                   codes_to_f16x2(hi01, 0x4140), codes_to_f16x2(hi01, 0x4342), pb0, pb1);
+        hmma_16816(o[c][1], codes_to_f16x2(lo23, 0x4140), codes_to_f16x2(lo23, 0x4342),
+                   codes_to_f16x2(hi23, 0x4140), codes_to_f16x2(hi23, 0x4342), pb0, pb1);
+      }
+    }
+
+    // ---- end of a (batch entry, CTA) segment: merge the 4 warps of each kv head ---------------
+    const bool last = (u + 1 == u1) || (find_batch(sm.prefix, B, u + 1) != ui.b);
+    if (last) {
+      float lt = l_run;
+      lt += __shfl_xor_sync(0xffffffffu, lt, 1);
+      lt += __shfl_xor_sync(0xffffffffu, lt, 2);
+      if (q == 0) {
+        sm.mrg_m[warp][g] = m_run;
+        sm.mrg_l[warp][g] = lt;
+      }
+      __syncthreads();
+      float f[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int hh = 2 * q + e;
+        float M = -INFINITY;
+#pragma unroll
+        for (int s2 = 0; s2 < 4; ++s2) M = fmaxf(M, sm.mrg_m[kh + 2 * s2][hh]);
+        const float mw = sm.mrg_m[warp][hh];
+        f[e] = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      }
+      float* scr = reinterpret_cast<float*>(sm.stage[buf]);  // [kh][sub][head][256]
+#pragma unroll
+      for (int c = 0; c < NB; ++c)
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int dim = group_dim(c, g, 2 * mt + (e >> 1));
+            const int hh = 2 * q + (e & 1);
+            scr[((kh * 4 + sub) * G + hh) * HD + dim] = o[c][mt][e] * f[e & 1];
+          }
+      __syncthreads();
+      const size_t slot = (size_t)blockIdx.x + ui.b;
+      for (int idx = tid; idx < NKV * G * HD; idx += THREADS) {
+        const int k2 = idx / (G * HD), rem = idx - k2 * (G * HD);
+        float acc = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < 4; ++s2) acc += scr[(k2 * 4 + s2) * G * HD + rem];
+        part.o[(slot * a.n_head + k2 * G) * HD + rem] = acc;
+      }
+      if (tid < NKV * G) {
+        const int k2 = tid / G, hh = tid % G;
+        float M = -INFINITY;
+#pragma unroll
+        for (int s2 = 0; s2 < 4; ++s2) M = fmaxf(M, sm.mrg_m[k2 + 2 * s2][hh]);
+        float L = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < 4; ++s2) {
+          const float mw = sm.mrg_m[k2 + 2 * s2][hh];
+          if (mw != -INFINITY) L = fmaf(sm.mrg_l[k2 + 2 * s2][hh], exp2f(mw - M), L);
+        }
+        part.m[slot * a.n_head + tid] = M;
+        part.l[slot * a.n_head + tid] = L;
+      }
+      fence_proxy_async_smem();  // scratch writes before the next bulk copy into this buffer
+      cur_b = -1;  // force re-initialisation for the next segment
+    }
+    __syncthreads();
+    if (tid == 0 && u + NS < u1) {
+      fence_proxy_async_smem();
+      issue(u + NS, buf);
+    }
+  }
+}
+
+// =============================================================================================
+// Combine kernels
+// =============================================================================================
+// Slot lists: mode 0 (generic) -> slots b*max_split + j, j < ceil(len/kGenChunk);
+//             mode 1 (fast)    -> slots i + b for CTAs i whose unit range meets entry b.
+// Writes normalised (out, gate) or, when m_out != nullptr, the merged (m, l, o) partial.
+__global__ void __launch_bounds__(256) decode_combine(DecodeArgs a, Partials part, int mode,
+                                                      int max_split, int n_cta,
+                                                      const float* gate, float* out,
+                                                      float* m_out, float* l_out, float* o_out) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int HD = a.nb * 32;
+  __shared__ long long red[2][256];
+  __shared__ int s_list[256];
+  __shared__ int s_n;
+  const int len = entry_len(a, b);
+  if (threadIdx.x == 0 && h == 0 && !entry_valid(a, b)) atomicOr(a.status, kStatusBadIndex);
+  if (mode == 1) {
+    // units before entry b and in total (block reduction over the batch)
+    long long before = 0, tot = 0;
+    for (int i = threadIdx.x; i < a.n_batch; i += blockDim.x) {
+      const long long un = (entry_len(a, i) + fast::ST - 1) / fast::ST;
+      tot += un;
+      if (i < b) before += un;
+    }
+    red[0][threadIdx.x] = before;
+    red[1][threadIdx.x] = tot;
+    __syncthreads();
+    for (int st = 128; st > 0; st >>= 1) {
+      if (threadIdx.x < st) {
+        red[0][threadIdx.x] += red[0][threadIdx.x + st];
+        red[1][threadIdx.x] += red[1][threadIdx.x + st];
+      }
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+      // CTA i of the split pass owned units [i*U/n_cta, (i+1)*U/n_cta) and wrote its share
+      // of entry b (if any) to slot i + b.
+      const long long U = red[1][0], P0 = red[0][0];
+      const long long P1 = P0 + (len + fast::ST - 1) / fast::ST;
+      int n = 0;
+      if (P1 > P0) {
+        long long ilo = ((P0 + 1) * n_cta + U - 1) / U - 1;
+        long long ihi = (P1 * n_cta + U - 1) / U - 1;
+        if (ilo < 0) ilo = 0;
+        if (ihi > n_cta - 1) ihi = n_cta - 1;
+        for (long long i = ilo; i <= ihi && n < 256; ++i) {
+          const long long r0 = i * U / n_cta, r1 = (i + 1) * U / n_cta;
+          if (max(r0, P0) < min(r1, P1)) s_list[n++] = (int)(i + b);
+        }
+      }
+      s_n = n;
+    }
+  } else if (threadIdx.x == 0) {
+    s_n = min((len + kGenChunk - 1) / kGenChunk, max_split);
+  }
+  __syncthreads();
+  const int n = s_n;
+  auto slot_of = [&](int k) -> size_t {
+    return mode == 1 ? (size_t)s_list[k] : (size_t)b * max_split + k;
+  };
+  float M = -INFINITY;
+  for (int k = 0; k < n; ++k) M = fmaxf(M, part.m[slot_of(k) * a.n_head + h]);
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int k = 0; k < n; ++k) {
+        const size_t sl = slot_of(k) * a.n_head + h;
+        const float mk = part.m[sl];
+        if (mk == -INFINITY) continue;
+        const float f = exp2f(mk - M);
+        L = fmaf(part.l[sl], f, L);
+        O = fmaf(part.o[sl * HD + d], f, O);
+      }
+    }
+    const size_t oi = ((size_t)b * a.n_head + h) * HD + d;
+    if (m_out) {
+      o_out[oi] = O;
+      if (d == 0) {
+        m_out[(size_t)b * a.n_head + h] = M;
+        l_out[(size_t)b * a.n_head + h] = L;
+      }
+    } else {
+      float r = L > 0.f ? O / L : 0.f;
+      if (gate) r *= 1.0f / (1.0f + expf(-gate[oi]));
+      if (!isfinite(r)) atomicOr(a.status, kStatusNonFinite);
+      out[oi] = r;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) lse_combine_kernel(int n_parts, int n_rows, int hd,
+                                                          const float* m, const float* l,
+                                                          const float* o, const float* gate,
+                                                          float* out, uint32_t* status) {
+  const int row = blockIdx.x;
+  float M = -INFINITY;
+  for (int k = 0; k < n_parts; ++k) M = fmaxf(M, m[(size_t)k * n_rows + row]);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY)
+      for (int k = 0; k < n_parts; ++k) {
+        const float mk = m[(size_t)k * n_rows + row];
+        if (mk == -INFINITY) continue;
+        const float f = exp2f(mk - M);
+        L = fmaf(l[(size_t)k * n_rows + row], f, L);
+        O = fmaf(o[((size_t)k * n_rows + row) * hd + d], f, O);
+      }
+    float r = L > 0.f ? O / L : 0.f;
+    const size_t oi = (size_t)row * hd + d;
+    if (gate) r *= 1.0f / (1.0f + expf(-gate[oi]));
+    if (!isfinite(r)) atomicOr(status, kStatusNonFinite);
+    out[oi] = r;
+  }
+}
+
+// =============================================================================================
+// Host launchers
+// =============================================================================================
+namespace {
+bool fast_applies(const DecodeArgs& a) {
+  return a.nb == fast::NB && a.n_kv == fast::NKV && a.n_head == fast::NKV * fast::G &&
+         a.n_batch <= fast::MAXB;
+}
+int heads_per_cta(int G) {
+  int hpc = 8;
+  while (hpc > 1 && G % hpc) hpc >>= 1;
+  return hpc;
+}
+template <int NB>
+cudaError_t launch_generic_nb(const DecodeArgs& a, const Partials& p, int max_split, int hpc,
+                              cudaStream_t st) {
+  dim3 grid(max_split, a.n_head / hpc, a.n_batch);
+  switch (hpc) {
+    case 8: decode_generic_split<NB, 8><<<grid, 128, 0, st>>>(a, p, max_split); break;
+    case 4: decode_generic_split<NB, 4><<<grid, 128, 0, st>>>(a, p, max_split); break;
+    case 2: decode_generic_split<NB, 2><<<grid, 128, 0, st>>>(a, p, max_split); break;
+    default: decode_generic_split<NB, 1><<<grid, 128, 0, st>>>(a, p, max_split); break;
+  }
+  return cudaGetLastError();
+}
+int generic_max_split(const DecodeArgs& a) {
+  return std::max(1, (a.max_ctx + kGenChunk - 1) / kGenChunk);
+}
+}  // namespace
+
+size_t decode_partial_floats(const DecodeArgs& a, int sm_count) {
+  size_t slots;
+  if (fast_applies(a)) slots = (size_t)sm_count + a.n_batch;
+  else slots = (size_t)a.n_batch * generic_max_split(a);
+  return slots * a.n_head * (2 + (size_t)a.nb * 32);
+}
+
+static cudaError_t run_split(const DecodeArgs& a, const Partials& p, int sm_count,
+                             int force_generic, cudaStream_t st, int* mode, int* max_split) {
+  if (!force_generic && fast_applies(a)) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 64 || !attr_set[dev]) {
+      e = cudaFuncSetAttribute(decode_fast_split, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)sizeof(fast::Smem));
+      if (e != cudaSuccess) return e;
+      if (dev < 64) attr_set[dev] = true;
+    }
+    *mode = 1;
+    *max_split = 0;
+    decode_fast_split<<<sm_count, fast::THREADS, sizeof(fast::Smem), st>>>(a, p);
+    return cudaGetLastError();
+  }
+  *mode = 0;
+  *max_split = generic_max_split(a);
+  const int hpc = heads_per_cta(a.n_head / a.n_kv);
+  switch (a.nb) {
+    case 1: return launch_generic_nb<1>(a, p, *max_split, hpc, st);
+    case 2: return launch_generic_nb<2>(a, p, *max_split, hpc, st);
+    case 4: return launch_generic_nb<4>(a, p, *max_split, hpc, st);
+    case 8: return launch_generic_nb<8>(a, p, *max_split, hpc, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_decode(const DecodeArgs& a, const Partials& part, const float* gate,
+                          float* out, int sm_count, int force_generic, cudaStream_t st,
+                          cudaEvent_t ev0, cudaEvent_t ev1) {
+  if (a.n_batch == 0) return cudaSuccess;
+  int mode = 0, max_split = 0;
+  if (ev0) cudaEventRecord(ev0, st);
+  cudaError_t e = run_split(a, part, sm_count, force_generic, st, &mode, &max_split);
+  if (e != cudaSuccess) return e;
+  if (ev1) cudaEventRecord(ev1, st);
+  decode_combine<<<dim3(a.n_batch, a.n_head), 256, 0, st>>>(a, part, mode, max_split, sm_count,
+                                                            gate, out, nullptr, nullptr, nullptr);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode_partial(const DecodeArgs& a, const Partials& part, float* m_out,
+                                  float* l_out, float* o_out, int sm_count, int force_generic,
+                                  cudaStream_t st) {
+  if (a.n_batch == 0) return cudaSuccess;
+  int mode = 0, max_split = 0;
+  cudaError_t e = run_split(a, part, sm_count, force_generic, st, &mode, &max_split);
+  if (e != cudaSuccess) return e;
+  decode_combine<<<dim3(a.n_batch, a.n_head), 256, 0, st>>>(a, part, mode, max_split, sm_count,
+                                                            nullptr, nullptr, m_out, l_out, o_out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lse_combine(int n_parts, int n_rows, int hd, const float* m, const float* l,
+                               const float* o, const float* gate, float* out, uint32_t* status,
+                               cudaStream_t st) {
+  if (n_rows == 0) return cudaSuccess;
+  lse_combine_kernel<<<n_rows, 256, 0, st>>>(n_parts, n_rows, hd, m, l, o, gate, out, status);
+  return cudaGetLastError();
+}
+
+}  // namespace vxg

@@ -1,0 +1,83 @@
+// Internal launch interface between the C-ABI host layer (abi.cu) and the kernels.
+#pragma once
+#include "common.cuh"
+
+namespace vxg {
+
+// q8_append.cu -----------------------------------------------------------------------------
+// For batch entry b and token t < n_tok: quantise k_new/v_new[b][t][n_kv][32*nb] into
+// sequence seq_ids[b] at position pos[b] + t.
+cudaError_t launch_q8_append(const int32_t* seq_ids, const int32_t* pos, const float* k_new,
+                             const float* v_new, uint8_t* k_pool, uint8_t* v_pool, int n_batch,
+                             int n_tok, int n_seq, int cap, int n_kv, int nb, uint32_t* status,
+                             cudaStream_t stream);
+
+// decode_attn.cu ---------------------------------------------------------------------------
+struct DecodeArgs {
+  const int32_t* seq_ids;  // [n_batch]
+  const int32_t* kv_begin; // [n_batch] first token attended (nullptr -> 0)
+  const int32_t* kv_end;   // [n_batch] one past the last token attended
+  const float* q;          // [n_batch][n_head][hd] prepared queries
+  const uint8_t* k_pool;   // [n_seq][cap][n_kv][nb] blocks
+  const uint8_t* v_pool;
+  int n_batch, n_seq, cap, n_head, n_kv, nb;
+  int end_add;             // effective end of entry b = kv_end[b] + end_add (decode: pos + 1)
+  int max_ctx;             // upper bound of (end - begin) over the batch (host-known)
+  float scale;             // softmax scale (1/sqrt(hd) in the reference)
+  uint32_t* status;
+};
+
+// Partial (m, l, o) buffers for the split-KV pass: m, l in log2 units, o unnormalised.
+struct Partials {
+  float* m;   // [n_slot][n_head]
+  float* l;   // [n_slot][n_head]
+  float* o;   // [n_slot][n_head][hd]
+  int n_slot; // slots available
+};
+
+// Bytes of partial storage the split-KV pass needs for these args.
+size_t decode_partial_floats(const DecodeArgs& a, int sm_count);
+
+// Split-KV pass then LSE combine into out[n_batch][n_head][hd] (gate optional, same shape).
+// `force_generic` selects the portable kernel even when the fast path applies.
+cudaError_t launch_decode(const DecodeArgs& a, const Partials& part, const float* gate,
+                          float* out, int sm_count, int force_generic, cudaStream_t stream,
+                          cudaEvent_t ev_split_begin, cudaEvent_t ev_split_end);
+
+// Split-KV pass only, leaving one combined (m, l, o) per (batch, head): m_out/l_out
+// [n_batch][n_head], o_out [n_batch][n_head][hd] (o unnormalised, m in log2 units).
+cudaError_t launch_decode_partial(const DecodeArgs& a, const Partials& part, float* m_out,
+                                  float* l_out, float* o_out, int sm_count, int force_generic,
+                                  cudaStream_t stream);
+
+// Log-sum-exp merge of n_parts partial results: m,l [n_parts][n_rows], o [n_parts][n_rows][hd]
+// -> out [n_rows][hd] (normalised, gate optional [n_rows][hd]).
+cudaError_t launch_lse_combine(int n_parts, int n_rows, int hd, const float* m, const float* l,
+                               const float* o, const float* gate, float* out, uint32_t* status,
+                               cudaStream_t stream);
+
+// deltanet.cu ------------------------------------------------------------------------------
+struct DeltaNetArgs {
+  const float* q;          // [n_batch][n_kh][dk] (before L2 norm)
+  const float* k;          // [n_batch][n_kh][dk]
+  const float* v;          // [n_batch][n_vh][dv]
+  const float* beta_raw;   // [n_batch][n_vh]
+  const float* alpha_raw;  // [n_batch][n_vh]
+  const float* ssm_a;      // [n_vh]
+  const float* dt_bias;    // [n_vh]
+  float* state;            // [n_batch][n_vh][dv][dk] updated in place
+  float* o;                // [n_batch][n_vh][dv]
+  int n_batch, n_kh, n_vh, dk, dv;
+  float eps, q_scale;
+  uint32_t* status;
+};
+cudaError_t launch_deltanet_step(const DeltaNetArgs& a, cudaStream_t stream);
+
+// prep.cu ----------------------------------------------------------------------------------
+// q/k prologue of step_full_gqa_q8 for one token: rope_cs = host-computed (cos, sin) pairs.
+cudaError_t launch_gqa_prep(const float* q_raw, float* k_cur, const float* q_norm,
+                            const float* k_norm, int gated, int n_head, int n_kv, int hd,
+                            const float2* rope_cs, int rope_half, int neox, float eps,
+                            float* q_out, float* gate_out, cudaStream_t stream);
+
+}  // namespace vxg
