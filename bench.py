@@ -157,7 +157,7 @@ def run_decode(args, world, rank, local):
 
     K, W = args.steps, args.warmup
     ctx = vxg_b200.Context()
-    batch = wl.DecodeBatch(seed=1 + 1000 * rank)
+    batch = wl.DecodeBatch(n_seq=args.seqs, ctx_hi=args.ctx_max, seed=1 + 1000 * rank)
     lens = batch.ctx_lens()
     n = batch.n_seq
     E2E_W = 2
@@ -234,8 +234,8 @@ def run_decode(args, world, rank, local):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
         "config": {
-            "workload": "config2: batched decode + Q8 append, 64 seqs per GPU, ctx U[1024,32768], "
-                        "16 q / 2 kv heads, head_dim 256, Q8_0 KV (34-B blocks)",
+            "workload": f"config2: batched decode + Q8 append, {n} seqs per GPU, ctx U[1024,"
+                        f"{batch.ctx_hi}], 16 q / 2 kv heads, head_dim 256, Q8_0 KV (34-B blocks)",
             "seqs_per_gpu": n, "mean_ctx": float(lens.mean()), "parallelism": f"seq-shard x{world}",
             "l2": "inputs larger than L2 (%.2f GB of KV read per step)" % (kv_bytes / 1e9),
             "hbm_gbs_whole_step": step_bytes / (ms_max / K * 1e-3) / 1e9,
@@ -454,6 +454,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "long", "deltanet"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seqs", type=int, default=64, help="sequences per GPU (profiling runs)")
+    ap.add_argument("--ctx-max", type=int, default=32768, help="context upper bound (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -89,7 +89,7 @@ VXG_ATTN_API int vxg_attn_cuda_memcpy(void* ctx, void* dst, const void* src, siz
 /* Replaces the per-layer Vec<KvQ8Block> pair of LlmState (crates/vxg-tensor/src/llm.rs:36-41,
  * 290-338) and vxt_metal_cb4_fast_state_create (crates/vxg-tensor/src/metal_cb4_fast_ffi.rs:
  * 149-154): zero-filled device K and V pools of n_seq x cap_tokens tokens.  head_dim must be a
- * multiple of 32 (llm.rs:291). */
+ * multiple of 32 (llm.rs:291) and at most 256. */
 VXG_ATTN_API void* vxg_attn_cuda_kv_create(void* ctx, uint32_t n_seq, uint32_t n_head_kv, uint32_t head_dim,
                               uint32_t cap_tokens, char* err, size_t cap);
 VXG_ATTN_API void vxg_attn_cuda_kv_destroy(void* kv);

@@ -12,9 +12,10 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100 GPU (B200)")
 
 
-@pytest.fixture(scope="session")
+@pytest.fixture
 def ctx():
-    """One library context on cuda:0 for the GPU tests (fails loudly without the library)."""
+    """A fresh library context on cuda:0 per test (fails loudly without the library), so a
+    context poisoned by one test's failure does not take the others down."""
     import torch
     torch.cuda.set_device(0)
     torch.cuda.init()

@@ -11,6 +11,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -80,10 +81,12 @@ struct Ctx {
   DevBuf part;                  // split-KV partials
   DevBuf io;                    // device staging for host-memory calls
   DevBuf aux;                   // prepared q / gate / rope table for the drop-in step
+  std::set<struct Kv*> pools;   // KV pools created on this context (orphaned on destroy)
 };
 
 struct Kv {
-  Ctx* ctx = nullptr;
+  Ctx* ctx = nullptr;           // nullptr once the owning context has been destroyed
+  int device = 0;
   uint32_t n_seq = 0, n_kv = 0, hd = 0, cap = 0;
   uint8_t* k = nullptr;
   uint8_t* v = nullptr;
@@ -98,6 +101,14 @@ Ctx& use_ctx(void* h) {
     throw AbiError(VXG_ATTN_ERR_INTERNAL, "context poisoned by an earlier device error: " + c.poison);
   check(cudaSetDevice(c.device), "cudaSetDevice");
   return c;
+}
+
+Kv& use_kv(Ctx& c, void* h) {
+  require(h != nullptr, VXG_ATTN_ERR_NULL_PTR, "null KV pool");
+  Kv& kv = *static_cast<Kv*>(h);
+  require(kv.device == c.device, VXG_ATTN_ERR_INVALID_OPTION,
+          "the KV pool lives on another device than this context");
+  return kv;
 }
 
 // Runs `body` with the reference's error discipline.
@@ -310,6 +321,8 @@ void vxg_attn_cuda_destroy(void* h) {
   Ctx* c = static_cast<Ctx*>(h);
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
+  for (Kv* kv : c->pools) kv->ctx = nullptr;  // pools outlive the context as plain memory
+  c->pools.clear();
   for (auto e : c->ev) cudaEventDestroy(e);
   c->part.release();
   c->io.release();
@@ -415,12 +428,15 @@ void* vxg_attn_cuda_kv_create(void* ctx, uint32_t n_seq, uint32_t n_head_kv, uin
     Ctx& c = use_ctx(ctx);
     require(n_seq > 0 && n_head_kv > 0 && cap_tokens > 0, VXG_ATTN_ERR_INVALID_OPTION,
             "n_seq, n_head_kv and cap_tokens must be positive");
-    require(head_dim > 0 && head_dim % 32 == 0 && head_dim <= 1024, VXG_ATTN_ERR_UNSUPPORTED,
+    require(head_dim > 0 && head_dim % 32 == 0, VXG_ATTN_ERR_UNSUPPORTED,
             "Q8_0 KV needs head_dim % 32 == 0 (llm.rs:291)");
+    require(head_dim <= 256, VXG_ATTN_ERR_UNSUPPORTED, "head_dim above 256 is not supported");
     require((uint64_t)n_seq * cap_tokens < (1ull << 31), VXG_ATTN_ERR_INVALID_OPTION,
             "n_seq * cap_tokens too large");
     kv = new Kv();
     kv->ctx = &c;
+    kv->device = c.device;
+    c.pools.insert(kv);
     kv->n_seq = n_seq;
     kv->n_kv = n_head_kv;
     kv->hd = head_dim;
@@ -443,9 +459,10 @@ void* vxg_attn_cuda_kv_create(void* ctx, uint32_t n_seq, uint32_t n_head_kv, uin
 void vxg_attn_cuda_kv_destroy(void* h) {
   if (!h) return;
   Kv* kv = static_cast<Kv*>(h);
+  cudaSetDevice(kv->device);
   if (kv->ctx) {
-    cudaSetDevice(kv->ctx->device);
     cudaStreamSynchronize(kv->ctx->stream);
+    kv->ctx->pools.erase(kv);
   }
   if (kv->k) cudaFree(kv->k);
   if (kv->v) cudaFree(kv->v);
@@ -464,6 +481,7 @@ int vxg_attn_cuda_kv_reserve(void* h, uint32_t cap_tokens, char* err, size_t cap
   Kv* kv = static_cast<Kv*>(h);
   return guarded(kv ? kv->ctx : nullptr, nullptr, err, cap, [&] {
     require(kv != nullptr, VXG_ATTN_ERR_NULL_PTR, "null KV pool");
+    require(kv->ctx != nullptr, VXG_ATTN_ERR_NULL_PTR, "the KV pool's context was destroyed");
     Ctx& c = use_ctx(kv->ctx);
     if (cap_tokens <= kv->cap) return VXG_ATTN_OK;
     // doubling with headroom, as native/metal_cb4_fast.h:174-191
@@ -508,8 +526,7 @@ static int kv_copy(void* ctx, void* h, uint32_t seq, uint32_t tok_begin, uint32_
                    char* err, size_t cap) {
   return guarded(ctx, nullptr, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
-    require(h != nullptr, VXG_ATTN_ERR_NULL_PTR, "null KV pool");
-    Kv& kv = *static_cast<Kv*>(h);
+    Kv& kv = use_kv(c, h);
     require(seq < kv.n_seq, VXG_ATTN_ERR_INVALID_OPTION, "sequence id out of range");
     require((uint64_t)tok_begin + n_tok <= kv.cap, VXG_ATTN_ERR_BUFFER_TOO_SMALL,
             "token range beyond the KV capacity");
@@ -557,8 +574,7 @@ int vxg_attn_cuda_q8_append(void* ctx, void* h, uint32_t n_batch, uint32_t n_tok
                             const float* v_new, int memkind, void* stream, char* err, size_t cap) {
   return guarded(ctx, stream, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
-    require(h != nullptr, VXG_ATTN_ERR_NULL_PTR, "null KV pool");
-    Kv& kv = *static_cast<Kv*>(h);
+    Kv& kv = use_kv(c, h);
     if (n_batch == 0 || n_tok == 0) return VXG_ATTN_OK;
     require(seq_ids && pos && k_new && v_new, VXG_ATTN_ERR_NULL_PTR, "null input");
     const bool host = memkind == VXG_ATTN_MEM_HOST;
@@ -586,8 +602,7 @@ int vxg_attn_cuda_q8_decode(void* ctx, void* h, uint32_t n_batch, uint32_t n_hea
                             char* err, size_t cap) {
   return guarded(ctx, stream, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
-    require(h != nullptr, VXG_ATTN_ERR_NULL_PTR, "null KV pool");
-    Kv& kv = *static_cast<Kv*>(h);
+    Kv& kv = use_kv(c, h);
     if (n_batch == 0) return VXG_ATTN_OK;
     require(seq_ids && pos && q && out, VXG_ATTN_ERR_NULL_PTR, "null input");
     require((k_new == nullptr) == (v_new == nullptr), VXG_ATTN_ERR_NULL_PTR,
@@ -631,8 +646,7 @@ int vxg_attn_cuda_q8_decode_partial(void* ctx, void* h, uint32_t n_batch, uint32
                                     void* stream, char* err, size_t cap) {
   return guarded(ctx, stream, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
-    require(h != nullptr, VXG_ATTN_ERR_NULL_PTR, "null KV pool");
-    Kv& kv = *static_cast<Kv*>(h);
+    Kv& kv = use_kv(c, h);
     if (n_batch == 0) return VXG_ATTN_OK;
     require(seq_ids && kv_begin && kv_end && q && m && l && o, VXG_ATTN_ERR_NULL_PTR,
             "null input");
@@ -699,8 +713,7 @@ int vxg_attn_cuda_step_full_gqa_q8(void* ctx, void* h, uint32_t seq, const float
                                    size_t cap) {
   return guarded(ctx, nullptr, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
-    require(h != nullptr, VXG_ATTN_ERR_NULL_PTR, "null KV pool");
-    Kv& kv = *static_cast<Kv*>(h);
+    Kv& kv = use_kv(c, h);
     require(q_raw && k_cur && v_cur && attn_out, VXG_ATTN_ERR_NULL_PTR, "null input");
     require(n_head_kv == kv.n_kv && head_dim == kv.hd, VXG_ATTN_ERR_INVALID_OPTION,
             "n_head_kv / head_dim differ from the KV pool's");

@@ -142,18 +142,17 @@ constexpr int TOKB = NKV * REC;    // 544 B per token in one cache
 constexpr int ST = 64;             // tokens per unit / stage
 constexpr int NS = 3;              // stages in flight
 constexpr int STB = ST * TOKB;     // 34816 B per stage per cache
-constexpr int THREADS = 256;       // 8 warps = 2 kv heads x 4 sub-tiles of 16 tokens
-constexpr int SROW = ST + 2;       // scale row stride (floats): conflict-free, 8-B aligned
+constexpr int WARPS = 8;           // (kv head, 16-token sub-tile)
+constexpr int THREADS = WARPS * 32;
+constexpr int SUBS = 4;            // 16-token sub-tiles per stage = partial slots per segment
 constexpr int MAXB = 1024;         // batch entries per launch
 constexpr uint32_t kWaitIters = 1u << 26;
 
 struct __align__(128) Smem {
   uint8_t stage[NS][2][STB];       // [buf][K, V][token][kv head][block] raw KvQ8Blocks
-  float sk[NKV * NB][SROW];        // K scales of the current stage, [kv head * 8 + block][token]
-  float sv[NKV * NB][SROW];        // V scales
-  float mrg_m[8][G];
-  float mrg_l[8][G];
-  long long prefix[MAXB + 1];      // units before batch entry b
+  float wsc[WARPS][2][4][NB][4];   // per-warp K/V scales: [q][block][tokens 2q,2q+1,2q+8,2q+9]
+  int prefix[MAXB + 1];            // units before batch entry b
+  unsigned done[NS];               // warps finished with each buffer
   uint64_t full[NS];
 };
 }  // namespace fast
@@ -176,9 +175,9 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 //   odd c : group r = codes 4r .. 4r+3
 //   even c: group r (r >= 1) = codes 4r-2 .. 4r+1; group 0 = codes {0, 1, 30, 31}
 // The MMA reduction order inside a block is free, so queries are permuted the same way.
-template <int C>
+template <int ODD>
 __device__ __forceinline__ uint32_t load_group(const uint8_t* blk, int r) {
-  if (C & 1) return lds32(blk + 2 + 4 * r);
+  if (ODD) return lds32(blk + 2 + 4 * r);
   uint32_t w = lds32(blk + 4 * r);
   if (r == 0) w = prmt(w, lds32(blk + 32), 0x5432);
   return w;
@@ -211,14 +210,16 @@ __device__ __forceinline__ void hmma_16816(float (&d)[4], uint32_t a0, uint32_t 
 // 1024 + x + 128, minus 1152.
 __device__ __forceinline__ uint32_t codes_to_f16x2(uint32_t pair_bytes, uint32_t sel) {
   const uint32_t h = prmt(pair_bytes, 0x64646464u, sel);
-  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __halves2half2(
-                                                                       __ushort_as_half(0x6480),
-                                                                       __ushort_as_half(0x6480)));
+  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h),
+                            __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
   return *reinterpret_cast<const uint32_t*>(&r);
 }
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 struct UnitInfo {
@@ -228,7 +229,7 @@ struct UnitInfo {
   int s;             // sequence id
 };
 
-__device__ __forceinline__ int find_batch(const long long* prefix, int B, long long u) {
+__device__ __forceinline__ int find_batch(const int* prefix, int B, int u) {
   int lo = 0, hi = B - 1;  // largest b with prefix[b] <= u
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -236,18 +237,6 @@ __device__ __forceinline__ int find_batch(const long long* prefix, int B, long l
     else hi = mid - 1;
   }
   return lo;
-}
-
-__device__ __forceinline__ UnitInfo unit_info(const DecodeArgs& a, const long long* prefix,
-                                              long long u) {
-  UnitInfo r;
-  r.b = find_batch(prefix, a.n_batch, u);
-  const int beg = a.kv_begin ? a.kv_begin[r.b] : 0;
-  const int end = a.kv_end[r.b] + a.end_add;
-  r.t_start = beg + (int)(u - prefix[r.b]) * fast::ST;
-  r.ntok = min(fast::ST, end - r.t_start);
-  r.s = a.seq_ids[r.b];
-  return r;
 }
 
 __device__ __forceinline__ bool entry_valid(const DecodeArgs& a, int b) {
@@ -262,6 +251,23 @@ __device__ __forceinline__ int entry_len(const DecodeArgs& a, int b) {
   return a.kv_end[b] + a.end_add - (a.kv_begin ? a.kv_begin[b] : 0);
 }
 
+__device__ __forceinline__ UnitInfo unit_info(const DecodeArgs& a, const int* prefix, int u) {
+  UnitInfo r;
+  r.b = find_batch(prefix, a.n_batch, u);
+  const int beg = a.kv_begin ? a.kv_begin[r.b] : 0;
+  const int end = a.kv_end[r.b] + a.end_add;
+  r.t_start = beg + (u - prefix[r.b]) * fast::ST;
+  r.ntok = min(fast::ST, end - r.t_start);
+  r.s = a.seq_ids[r.b];
+  return r;
+}
+
+// Warp roles: warp = kv head (bit 0) | 16-token sub-tile (bits 1-2).  Warps only meet at the
+// stage ring: each waits for a stage's bulk copy, and the last warp done with a buffer refills
+// it, so warps drift freely within the ring (no block-wide barrier in the steady state).  At
+// the end of a (batch entry, CTA) segment every warp writes its own (m, l, O) partial; the
+// combine kernel merges them.  Partial slot of warp (kh, sub) in CTA i for entry b:
+// (i + b) * SUBS + sub, heads kh*8 .. kh*8+7, O stored [dim][head].
 __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs a,
                                                                        Partials part) {
   using namespace fast;
@@ -275,18 +281,18 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
   // ---- unit prefix over the batch (warp 0: serial per lane chunk + warp scan) -----------
   if (warp == 0) {
     const int per = (B + 31) / 32;
-    long long run = 0;
+    int run = 0;
     for (int i = 0; i < per; ++i) {
       const int bb = lane * per + i;
       if (bb < B) run += (entry_len(a, bb) + ST - 1) / ST;
     }
-    long long incl = run;
+    int incl = run;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const long long v = __shfl_up_sync(0xffffffffu, incl, o);
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += v;
     }
-    long long acc = incl - run;
+    int acc = incl - run;
     for (int i = 0; i < per; ++i) {
       const int bb = lane * per + i;
       if (bb < B) {
@@ -297,16 +303,19 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
     if (lane == 31) sm.prefix[B] = incl;
   }
   if (tid == 0) {
-    for (int i = 0; i < NS; ++i) mbar_init(&sm.full[i], 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&sm.full[i], 1);
+      sm.done[i] = 0;
+    }
     fence_mbar_init();
   }
   __syncthreads();
   const long long U = sm.prefix[B];
-  const long long u0 = (long long)blockIdx.x * U / gridDim.x;
-  const long long u1 = (long long)(blockIdx.x + 1) * U / gridDim.x;
+  const int u0 = (int)((long long)blockIdx.x * U / gridDim.x);
+  const int u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
   if (u0 >= u1) return;
 
-  auto issue = [&](long long u, int buf) {
+  auto issue = [&](int u, int buf) {
     const UnitInfo ui = unit_info(a, sm.prefix, u);
     const uint32_t bytes = (uint32_t)ui.ntok * TOKB;
     const size_t off = ((size_t)ui.s * a.cap + ui.t_start) * TOKB;
@@ -321,18 +330,30 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
   float fac = 0.f;         // per-head factor sigma/254 * scale * log2(e) (head g)
   float o[NB][2][4];       // O^T accumulators: [block][m-tile][frag]
   float m_run = -INFINITY, l_run = 0.f;
-  int cur_b = -1;
+  // current batch entry (incremental walk over the units)
+  int b = find_batch(sm.prefix, B, u0);
+  int seg_new = 1;
+  int e_beg = 0, e_end = 0, e_seq = 0;
+  const float4* wsk = reinterpret_cast<const float4*>(&sm.wsc[warp][0][q][0][0]);
+  const float4* wsv = reinterpret_cast<const float4*>(&sm.wsc[warp][1][q][0][0]);
+  const int swk = g >> 2;   // K load order swizzle (bank conflicts between tokens g and g+4)
+  const int swv = q >> 1;   // V load order swizzle (tokens 2q and 2q+4)
 
-  for (long long u = u0; u < u1; ++u) {
-    const int it = (int)(u - u0);
+  for (int u = u0; u < u1; ++u) {
+    const int it = u - u0;
     const int buf = it % NS;
     const uint32_t par = (uint32_t)(it / NS) & 1u;
-    const UnitInfo ui = unit_info(a, sm.prefix, u);
-
-    if (ui.b != cur_b) {
+    while (u >= sm.prefix[b + 1]) {
+      ++b;
+      seg_new = 1;
+    }
+    if (seg_new) {
+      seg_new = 0;
+      e_seq = a.seq_ids[b];
+      e_beg = a.kv_begin ? a.kv_begin[b] : 0;
+      e_end = a.kv_end[b] + a.end_add;
       // ---- query digits: q ~= sigma * (d_a + d_b / 254), sigma = max|q| / 127 ------------
-      cur_b = ui.b;
-      const float* qh = a.q + ((size_t)ui.b * a.n_head + kh * G + g) * HD;
+      const float* qh = a.q + ((size_t)b * a.n_head + kh * G + g) * HD;
       float amax = 0.f;
       bool nonfinite = false;
 #pragma unroll
@@ -379,12 +400,13 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
 #pragma unroll
           for (int e = 0; e < 4; ++e) o[c][mt][e] = 0.f;
     }
+    const int t_start = e_beg + (u - sm.prefix[b]) * ST;
+    const int ntok = min(ST, e_end - t_start);
 
-    // ---- wait for this stage (bounded) ----------------------------------------------------
-    const bool ok = __syncthreads_and(mbar_wait(&sm.full[buf], par, kWaitIters));
-    if (!ok) {
+    // ---- wait for this stage (bounded, per warp) -------------------------------------------
+    if (!mbar_wait(&sm.full[buf], par, kWaitIters)) {
       // Give up: flag it, let the copies this CTA issued land (bounded), then leave.
-      if (tid == 0) atomicOr(a.status, kStatusTimeout);
+      if (lane == 0) atomicOr(a.status, kStatusTimeout);
       for (int k = 1; k < NS; ++k)
         if (u + k < u1) mbar_wait(&sm.full[(it + k) % NS], (uint32_t)((it + k) / NS) & 1u, kWaitIters);
       return;
@@ -392,43 +414,51 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
     const uint8_t* kst = sm.stage[buf][0];
     const uint8_t* vst = sm.stage[buf][1];
 
-    // ---- scales of the stage to f32 (0 for tokens past the unit) ---------------------------
+    if (16 * sub < ntok) {
+      // ---- this warp's scales as f32 (0 past the unit) ----------------------------------------
+      {
+        const int which = lane >> 4, qq = (lane >> 2) & 3, cp = lane & 3;
+        const uint8_t* src = (which ? vst : kst) + kh * REC;
 #pragma unroll
-    for (int r = 0; r < (2 * NKV * NB * ST) / THREADS; ++r) {
-      const int e = tid + r * THREADS;
-      const int c = e & 7, hh = (e >> 3) & 1, t = (e >> 4) & (ST - 1), which = e >> 10;
-      const uint8_t* base = (which ? vst : kst) + t * TOKB + hh * REC + c * kBlk;
-      const float d = t < ui.ntok ? f16bits_to_f32(*reinterpret_cast<const uint16_t*>(base)) : 0.f;
-      (which ? sm.sv : sm.sk)[hh * NB + c][t] = d;
-    }
-    __syncthreads();
-
-    if (16 * sub < ui.ntok) {
-      // ---- S = Q K^T on int8 tensor cores: 2 n-tiles of 8 tokens -----------------------------
-      float sacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * cp + cc;
+          float4 d;
+          float* dp = &d.x;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint8_t* rec = kst + (16 * sub + 8 * j + g) * TOKB + kh * REC;
-#pragma unroll
-        for (int c = 0; c < NB; ++c) {
-          uint32_t b0, b1;
-          switch (c) {
-            case 0: b0 = load_group<0>(rec, 2 * q); b1 = load_group<0>(rec, 2 * q + 1); break;
-            case 1: b0 = load_group<1>(rec + 1 * kBlk, 2 * q); b1 = load_group<1>(rec + 1 * kBlk, 2 * q + 1); break;
-            case 2: b0 = load_group<0>(rec + 2 * kBlk, 2 * q); b1 = load_group<0>(rec + 2 * kBlk, 2 * q + 1); break;
-            case 3: b0 = load_group<1>(rec + 3 * kBlk, 2 * q); b1 = load_group<1>(rec + 3 * kBlk, 2 * q + 1); break;
-            case 4: b0 = load_group<0>(rec + 4 * kBlk, 2 * q); b1 = load_group<0>(rec + 4 * kBlk, 2 * q + 1); break;
-            case 5: b0 = load_group<1>(rec + 5 * kBlk, 2 * q); b1 = load_group<1>(rec + 5 * kBlk, 2 * q + 1); break;
-            case 6: b0 = load_group<0>(rec + 6 * kBlk, 2 * q); b1 = load_group<0>(rec + 6 * kBlk, 2 * q + 1); break;
-            default: b0 = load_group<1>(rec + 7 * kBlk, 2 * q); b1 = load_group<1>(rec + 7 * kBlk, 2 * q + 1); break;
+          for (int i = 0; i < 4; ++i) {
+            const int tok = 16 * sub + 2 * qq + (i & 1) + 8 * (i >> 1);
+            dp[i] = tok < ntok
+                        ? f16bits_to_f32(*reinterpret_cast<const uint16_t*>(src + tok * TOKB + c * kBlk))
+                        : 0.f;
           }
+          *reinterpret_cast<float4*>(&sm.wsc[warp][which][qq][c][0]) = d;
+        }
+      }
+      __syncwarp();
+      // ---- S = Q K^T on int8 tensor cores: 2 n-tiles of 8 tokens ---------------------------
+      float sacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+      const uint8_t* rec0 = kst + (16 * sub + g) * TOKB + kh * REC;
+#pragma unroll
+      for (int c = 0; c < NB; ++c) {
+        const float4 dk = wsk[c];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const uint8_t* blk = rec0 + 8 * j * TOKB + c * kBlk;
+          uint32_t x, y;
+          if (c & 1) {
+            x = load_group<1>(blk, 2 * q + swk);
+            y = load_group<1>(blk, 2 * q + 1 - swk);
+          } else {
+            x = load_group<0>(blk, 2 * q + swk);
+            y = load_group<0>(blk, 2 * q + 1 - swk);
+          }
+          const uint32_t b0 = swk ? y : x, b1 = swk ? x : y;
           int acc[4];
           imma_16832(acc, qa[c], b0, b1);
           const int x0 = 254 * acc[0] + acc[2];
           const int x1 = 254 * acc[1] + acc[3];
-          const float2 d = *reinterpret_cast<const float2*>(&sm.sk[kh * NB + c][16 * sub + 8 * j + 2 * q]);
-          sacc[j][0] = fmaf(d.x, __int2float_rn(x0), sacc[j][0]);
-          sacc[j][1] = fmaf(d.y, __int2float_rn(x1), sacc[j][1]);
+          sacc[j][0] = fmaf(j ? dk.z : dk.x, __int2float_rn(x0), sacc[j][0]);
+          sacc[j][1] = fmaf(j ? dk.w : dk.y, __int2float_rn(x1), sacc[j][1]);
         }
       }
       // ---- online softmax (log2 domain) ----------------------------------------------------
@@ -439,21 +469,22 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int tl = 16 * sub + 8 * j + 2 * q + e;
-          p[j][e] = tl < ui.ntok ? sacc[j][e] * fac : -INFINITY;
+          p[j][e] = tl < ntok ? sacc[j][e] * fac : -INFINITY;
           mx = fmaxf(mx, p[j][e]);
         }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      if (fac != fac) mx = 0.f;  // keep the running max finite so the NaN survives the merge
+      // Token 16*sub is always valid, so -inf here means every valid score is NaN (a
+      // non-finite query): keep the running max finite so the NaN survives the merges.
+      if (mx == -INFINITY) mx = 0.f;
       const float m_new = fmaxf(m_run, mx);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m_run - m_use);
+      const float alpha = exp2f(m_run - m_new);
       float ps = 0.f;
 #pragma unroll
       for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          p[j][e] = exp2f(p[j][e] - m_use);
+          p[j][e] = exp2f(p[j][e] - m_new);
           ps += p[j][e];
         }
       l_run = fmaf(l_run, alpha, ps);
@@ -472,30 +503,27 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
           }
       }
       // ---- O^T += V^T P'^T on f16 tensor cores, P' = p * d_v ---------------------------------
-      const uint8_t* vrec = vst + (16 * sub + 2 * q) * TOKB + kh * REC;
+      const uint8_t* vr0 = vst + (16 * sub + 2 * q + swv) * TOKB + kh * REC;      // first
+      const uint8_t* vr1 = vst + (16 * sub + 2 * q + 1 - swv) * TOKB + kh * REC;  // second
 #pragma unroll
       for (int c = 0; c < NB; ++c) {
-        const float2 dv0 = *reinterpret_cast<const float2*>(&sm.sv[kh * NB + c][16 * sub + 2 * q]);
-        const float2 dv8 = *reinterpret_cast<const float2*>(&sm.sv[kh * NB + c][16 * sub + 8 + 2 * q]);
-        const uint32_t pb0 = pack_f16x2(p[0][0] * dv0.x, p[0][1] * dv0.y);
-        const uint32_t pb1 = pack_f16x2(p[1][0] * dv8.x, p[1][1] * dv8.y);
-        const uint8_t* bp = vrec + c * kBlk;
-        uint32_t w0, w1, w8, w9;
+        const float4 dv = wsv[c];
+        const uint32_t pb0 = pack_f16x2(p[0][0] * dv.x, p[0][1] * dv.y);
+        const uint32_t pb1 = pack_f16x2(p[1][0] * dv.z, p[1][1] * dv.w);
+        uint32_t f0, f1, f8, f9;
         if (c & 1) {
-          w0 = load_group<1>(bp, g);
-          w1 = load_group<1>(bp + TOKB, g);
-          w8 = load_group<1>(bp + 8 * TOKB, g);
-          w9 = load_group<1>(bp + 9 * TOKB, g);
+          f0 = load_group<1>(vr0 + c * kBlk, g);
+          f1 = load_group<1>(vr1 + c * kBlk, g);
+          f8 = load_group<1>(vr0 + 8 * TOKB + c * kBlk, g);
+          f9 = load_group<1>(vr1 + 8 * TOKB + c * kBlk, g);
         } else {
-          w0 = load_group<0>(bp, g);
-          w1 = load_group<0>(bp + TOKB, g);
-          w8 = load_group<0>(bp + 8 * TOKB, g);
-          w9 = load_group<0>(bp + 9 * TOKB, g);
+          f0 = load_group<0>(vr0 + c * kBlk, g);
+          f1 = load_group<0>(vr1 + c * kBlk, g);
+          f8 = load_group<0>(vr0 + 8 * TOKB + c * kBlk, g);
+          f9 = load_group<0>(vr1 + 8 * TOKB + c * kBlk, g);
         }
-        w0 ^= 0x80808080u;
-        w1 ^= 0x80808080u;
-        w8 ^= 0x80808080u;
-        w9 ^= 0x80808080u;
+        const uint32_t w0 = (swv ? f1 : f0) ^ 0x80808080u, w1 = (swv ? f0 : f1) ^ 0x80808080u;
+        const uint32_t w8 = (swv ? f9 : f8) ^ 0x80808080u, w9 = (swv ? f8 : f9) ^ 0x80808080u;
         const uint32_t lo01 = prmt(w0, w1, 0x5140), lo23 = prmt(w0, w1, 0x7362);
         const uint32_t hi01 = prmt(w8, w9, 0x5140), hi23 = prmt(w8, w9, 0x7362);
         hmma_16816(o[c][0], codes_to_f16x2(lo01, 0x4140), codes_to_f16x2(lo01, 0x4342),
@@ -505,68 +533,43 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
       }
     }
 
-    // ---- end of a (batch entry, CTA) segment: merge the 4 warps of each kv head ---------------
-    const bool last = (u + 1 == u1) || (find_batch(sm.prefix, B, u + 1) != ui.b);
-    if (last) {
+    // ---- release the buffer; the last warp out refills it ------------------------------------
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      const unsigned prev = atomicAdd(&sm.done[buf], 1u);
+      if (prev == WARPS - 1) {
+        sm.done[buf] = 0;
+        __threadfence_block();
+        if (u + NS < u1) {
+          fence_proxy_async_smem();
+          issue(u + NS, buf);
+        }
+      }
+    }
+
+    // ---- end of this (batch entry, CTA) segment: write this warp's partial -----------------
+    if (u + 1 == u1 || u + 1 >= sm.prefix[b + 1]) {
+      const size_t slot = ((size_t)blockIdx.x + b) * SUBS + sub;
       float lt = l_run;
       lt += __shfl_xor_sync(0xffffffffu, lt, 1);
       lt += __shfl_xor_sync(0xffffffffu, lt, 2);
       if (q == 0) {
-        sm.mrg_m[warp][g] = m_run;
-        sm.mrg_l[warp][g] = lt;
+        part.m[slot * a.n_head + kh * G + g] = m_run;
+        part.l[slot * a.n_head + kh * G + g] = lt;
       }
-      __syncthreads();
-      float f[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int hh = 2 * q + e;
-        float M = -INFINITY;
-#pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2) M = fmaxf(M, sm.mrg_m[kh + 2 * s2][hh]);
-        const float mw = sm.mrg_m[warp][hh];
-        f[e] = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
-      }
-      float* scr = reinterpret_cast<float*>(sm.stage[buf]);  // [kh][sub][head][256]
+      float* po = part.o + slot * a.n_head * HD + kh * G + 2 * q;   // [dim][head]
 #pragma unroll
       for (int c = 0; c < NB; ++c)
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int dim = group_dim(c, g, 2 * mt + (e >> 1));
-            const int hh = 2 * q + (e & 1);
-            scr[((kh * 4 + sub) * G + hh) * HD + dim] = o[c][mt][e] * f[e & 1];
+          for (int r = 0; r < 2; ++r) {
+            const int dim = group_dim(c, g, 2 * mt + r);
+            *reinterpret_cast<float2*>(po + (size_t)dim * a.n_head) =
+                make_float2(o[c][mt][2 * r], o[c][mt][2 * r + 1]);
           }
-      __syncthreads();
-      const size_t slot = (size_t)blockIdx.x + ui.b;
-      for (int idx = tid; idx < NKV * G * HD; idx += THREADS) {
-        const int k2 = idx / (G * HD), rem = idx - k2 * (G * HD);
-        float acc = 0.f;
-#pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2) acc += scr[(k2 * 4 + s2) * G * HD + rem];
-        part.o[(slot * a.n_head + k2 * G) * HD + rem] = acc;
-      }
-      if (tid < NKV * G) {
-        const int k2 = tid / G, hh = tid % G;
-        float M = -INFINITY;
-#pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2) M = fmaxf(M, sm.mrg_m[k2 + 2 * s2][hh]);
-        float L = 0.f;
-#pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2) {
-          const float mw = sm.mrg_m[k2 + 2 * s2][hh];
-          if (mw != -INFINITY) L = fmaf(sm.mrg_l[k2 + 2 * s2][hh], exp2f(mw - M), L);
-        }
-        part.m[slot * a.n_head + tid] = M;
-        part.l[slot * a.n_head + tid] = L;
-      }
-      fence_proxy_async_smem();  // scratch writes before the next bulk copy into this buffer
-      cur_b = -1;  // force re-initialisation for the next segment
-    }
-    __syncthreads();
-    if (tid == 0 && u + NS < u1) {
-      fence_proxy_async_smem();
-      issue(u + NS, buf);
+      seg_new = 1;
     }
   }
 }
@@ -574,71 +577,23 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
 // =============================================================================================
 // Combine kernels
 // =============================================================================================
-// Slot lists: mode 0 (generic) -> slots b*max_split + j, j < ceil(len/kGenChunk);
-//             mode 1 (fast)    -> slots i + b for CTAs i whose unit range meets entry b.
+// Generic combine: slots b*max_split + j, j < min(ceil(len/kGenChunk), max_split), o [slot][head][dim].
 // Writes normalised (out, gate) or, when m_out != nullptr, the merged (m, l, o) partial.
-__global__ void __launch_bounds__(256) decode_combine(DecodeArgs a, Partials part, int mode,
-                                                      int max_split, int n_cta,
+__global__ void __launch_bounds__(256) decode_combine(DecodeArgs a, Partials part, int max_split,
                                                       const float* gate, float* out,
                                                       float* m_out, float* l_out, float* o_out) {
   const int b = blockIdx.x, h = blockIdx.y;
   const int HD = a.nb * 32;
-  __shared__ long long red[2][256];
-  __shared__ int s_list[256];
-  __shared__ int s_n;
   const int len = entry_len(a, b);
   if (threadIdx.x == 0 && h == 0 && !entry_valid(a, b)) atomicOr(a.status, kStatusBadIndex);
-  if (mode == 1) {
-    // units before entry b and in total (block reduction over the batch)
-    long long before = 0, tot = 0;
-    for (int i = threadIdx.x; i < a.n_batch; i += blockDim.x) {
-      const long long un = (entry_len(a, i) + fast::ST - 1) / fast::ST;
-      tot += un;
-      if (i < b) before += un;
-    }
-    red[0][threadIdx.x] = before;
-    red[1][threadIdx.x] = tot;
-    __syncthreads();
-    for (int st = 128; st > 0; st >>= 1) {
-      if (threadIdx.x < st) {
-        red[0][threadIdx.x] += red[0][threadIdx.x + st];
-        red[1][threadIdx.x] += red[1][threadIdx.x + st];
-      }
-      __syncthreads();
-    }
-    if (threadIdx.x == 0) {
-      // CTA i of the split pass owned units [i*U/n_cta, (i+1)*U/n_cta) and wrote its share
-      // of entry b (if any) to slot i + b.
-      const long long U = red[1][0], P0 = red[0][0];
-      const long long P1 = P0 + (len + fast::ST - 1) / fast::ST;
-      int n = 0;
-      if (P1 > P0) {
-        long long ilo = ((P0 + 1) * n_cta + U - 1) / U - 1;
-        long long ihi = (P1 * n_cta + U - 1) / U - 1;
-        if (ilo < 0) ilo = 0;
-        if (ihi > n_cta - 1) ihi = n_cta - 1;
-        for (long long i = ilo; i <= ihi && n < 256; ++i) {
-          const long long r0 = i * U / n_cta, r1 = (i + 1) * U / n_cta;
-          if (max(r0, P0) < min(r1, P1)) s_list[n++] = (int)(i + b);
-        }
-      }
-      s_n = n;
-    }
-  } else if (threadIdx.x == 0) {
-    s_n = min((len + kGenChunk - 1) / kGenChunk, max_split);
-  }
-  __syncthreads();
-  const int n = s_n;
-  auto slot_of = [&](int k) -> size_t {
-    return mode == 1 ? (size_t)s_list[k] : (size_t)b * max_split + k;
-  };
+  const int n = min((len + kGenChunk - 1) / kGenChunk, max_split);
   float M = -INFINITY;
-  for (int k = 0; k < n; ++k) M = fmaxf(M, part.m[slot_of(k) * a.n_head + h]);
+  for (int k = 0; k < n; ++k) M = fmaxf(M, part.m[((size_t)b * max_split + k) * a.n_head + h]);
   for (int d = threadIdx.x; d < HD; d += blockDim.x) {
     float L = 0.f, O = 0.f;
     if (M != -INFINITY) {
       for (int k = 0; k < n; ++k) {
-        const size_t sl = slot_of(k) * a.n_head + h;
+        const size_t sl = ((size_t)b * max_split + k) * a.n_head + h;
         const float mk = part.m[sl];
         if (mk == -INFINITY) continue;
         const float f = exp2f(mk - M);
@@ -654,7 +609,112 @@ __global__ void __launch_bounds__(256) decode_combine(DecodeArgs a, Partials par
         l_out[(size_t)b * a.n_head + h] = L;
       }
     } else {
-      float r = L > 0.f ? O / L : 0.f;
+      float r = (L > 0.f || L != L) ? O / L : 0.f;  // NaN partials stay NaN
+      if (gate) r *= 1.0f / (1.0f + expf(-gate[oi]));
+      if (!isfinite(r)) atomicOr(a.status, kStatusNonFinite);
+      out[oi] = r;
+    }
+  }
+}
+
+// Fast-path combine: one CTA per batch entry, thread = output dimension, all 16 heads.  CTA i
+// of the split pass owned units [i*U/n_cta, (i+1)*U/n_cta); for each such CTA meeting entry b,
+// slots (i + b)*SUBS + sub hold the partials of its 4 sub-tiles, o stored [dim][head].
+__global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partials part, int n_cta,
+                                                           const float* gate, float* out,
+                                                           float* m_out, float* l_out,
+                                                           float* o_out) {
+  using namespace fast;
+  constexpr int H = NKV * G;
+  const int b = blockIdx.x, d = threadIdx.x;
+  __shared__ long long red[2][256];
+  __shared__ int s_list[256];
+  __shared__ int s_n;
+  __shared__ float s_M[H], s_L[H];
+  const int len = entry_len(a, b);
+  if (d == 0 && !entry_valid(a, b)) atomicOr(a.status, kStatusBadIndex);
+  long long before = 0, tot = 0;
+  for (int i = d; i < a.n_batch; i += 256) {
+    const long long un = (entry_len(a, i) + ST - 1) / ST;
+    tot += un;
+    if (i < b) before += un;
+  }
+  red[0][d] = before;
+  red[1][d] = tot;
+  __syncthreads();
+  for (int st = 128; st > 0; st >>= 1) {
+    if (d < st) {
+      red[0][d] += red[0][d + st];
+      red[1][d] += red[1][d + st];
+    }
+    __syncthreads();
+  }
+  if (d == 0) {
+    const long long U = red[1][0], P0 = red[0][0];
+    const long long P1 = P0 + (len + ST - 1) / ST;
+    int n = 0;
+    if (P1 > P0) {
+      long long ilo = ((P0 + 1) * n_cta + U - 1) / U - 1;
+      long long ihi = (P1 * n_cta + U - 1) / U - 1;
+      if (ilo < 0) ilo = 0;
+      if (ihi > n_cta - 1) ihi = n_cta - 1;
+      for (long long i = ilo; i <= ihi && n < 256; ++i) {
+        const long long r0 = i * U / n_cta, r1 = (i + 1) * U / n_cta;
+        if (max(r0, P0) < min(r1, P1)) s_list[n++] = (int)(i + b);
+      }
+    }
+    s_n = n;
+  }
+  __syncthreads();
+  const int ns = s_n * SUBS;
+  if (d < H) {
+    float M = -INFINITY;
+    for (int k = 0; k < ns; ++k) {
+      const size_t sl = (size_t)s_list[k / SUBS] * SUBS + k % SUBS;
+      M = fmaxf(M, part.m[sl * H + d]);
+    }
+    float L = 0.f;
+    if (M != -INFINITY)
+      for (int k = 0; k < ns; ++k) {
+        const size_t sl = (size_t)s_list[k / SUBS] * SUBS + k % SUBS;
+        const float mk = part.m[sl * H + d];
+        if (mk != -INFINITY) L = fmaf(part.l[sl * H + d], exp2f(mk - M), L);
+      }
+    s_M[d] = M;
+    s_L[d] = L;
+  }
+  __syncthreads();
+  float acc[H];
+#pragma unroll
+  for (int h = 0; h < H; ++h) acc[h] = 0.f;
+  for (int k = 0; k < ns; ++k) {
+    const size_t sl = (size_t)s_list[k / SUBS] * SUBS + k % SUBS;
+    const float4* src = reinterpret_cast<const float4*>(part.o + (sl * HD + d) * H);
+#pragma unroll
+    for (int v = 0; v < H / 4; ++v) {
+      const float4 x = src[v];
+      const float* xp = &x.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = 4 * v + e;
+        const float mk = part.m[sl * H + h];
+        const float f = (mk == -INFINITY || s_M[h] == -INFINITY) ? 0.f : exp2f(mk - s_M[h]);
+        acc[h] = fmaf(xp[e], f, acc[h]);
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < H; ++h) {
+    const size_t oi = ((size_t)b * H + h) * HD + d;
+    if (m_out) {
+      o_out[oi] = acc[h];
+      if (d == 0) {
+        m_out[(size_t)b * H + h] = s_M[h];
+        l_out[(size_t)b * H + h] = s_L[h];
+      }
+    } else {
+      const float L = s_L[h];
+      float r = (L > 0.f || L != L) ? acc[h] / L : 0.f;  // NaN partials stay NaN
       if (gate) r *= 1.0f / (1.0f + expf(-gate[oi]));
       if (!isfinite(r)) atomicOr(a.status, kStatusNonFinite);
       out[oi] = r;
@@ -679,7 +739,7 @@ __global__ void __launch_bounds__(256) lse_combine_kernel(int n_parts, int n_row
         L = fmaf(l[(size_t)k * n_rows + row], f, L);
         O = fmaf(o[((size_t)k * n_rows + row) * hd + d], f, O);
       }
-    float r = L > 0.f ? O / L : 0.f;
+    float r = (L > 0.f || L != L) ? O / L : 0.f;  // NaN partials stay NaN
     const size_t oi = (size_t)row * hd + d;
     if (gate) r *= 1.0f / (1.0f + expf(-gate[oi]));
     if (!isfinite(r)) atomicOr(status, kStatusNonFinite);
@@ -719,7 +779,7 @@ int generic_max_split(const DecodeArgs& a) {
 
 size_t decode_partial_floats(const DecodeArgs& a, int sm_count) {
   size_t slots;
-  if (fast_applies(a)) slots = (size_t)sm_count + a.n_batch;
+  if (fast_applies(a)) slots = ((size_t)sm_count + a.n_batch) * fast::SUBS;
   else slots = (size_t)a.n_batch * generic_max_split(a);
   return slots * a.n_head * (2 + (size_t)a.nb * 32);
 }
@@ -748,7 +808,11 @@ static cudaError_t run_split(const DecodeArgs& a, const Partials& p, int sm_coun
   switch (a.nb) {
     case 1: return launch_generic_nb<1>(a, p, *max_split, hpc, st);
     case 2: return launch_generic_nb<2>(a, p, *max_split, hpc, st);
+    case 3: return launch_generic_nb<3>(a, p, *max_split, hpc, st);
     case 4: return launch_generic_nb<4>(a, p, *max_split, hpc, st);
+    case 5: return launch_generic_nb<5>(a, p, *max_split, hpc, st);
+    case 6: return launch_generic_nb<6>(a, p, *max_split, hpc, st);
+    case 7: return launch_generic_nb<7>(a, p, *max_split, hpc, st);
     case 8: return launch_generic_nb<8>(a, p, *max_split, hpc, st);
     default: return cudaErrorInvalidValue;
   }
@@ -763,8 +827,12 @@ cudaError_t launch_decode(const DecodeArgs& a, const Partials& part, const float
   cudaError_t e = run_split(a, part, sm_count, force_generic, st, &mode, &max_split);
   if (e != cudaSuccess) return e;
   if (ev1) cudaEventRecord(ev1, st);
-  decode_combine<<<dim3(a.n_batch, a.n_head), 256, 0, st>>>(a, part, mode, max_split, sm_count,
-                                                            gate, out, nullptr, nullptr, nullptr);
+  if (mode == 1)
+    decode_fast_combine<<<a.n_batch, 256, 0, st>>>(a, part, sm_count, gate, out, nullptr,
+                                                   nullptr, nullptr);
+  else
+    decode_combine<<<dim3(a.n_batch, a.n_head), 256, 0, st>>>(a, part, max_split, gate, out,
+                                                              nullptr, nullptr, nullptr);
   return cudaGetLastError();
 }
 
@@ -775,8 +843,12 @@ cudaError_t launch_decode_partial(const DecodeArgs& a, const Partials& part, flo
   int mode = 0, max_split = 0;
   cudaError_t e = run_split(a, part, sm_count, force_generic, st, &mode, &max_split);
   if (e != cudaSuccess) return e;
-  decode_combine<<<dim3(a.n_batch, a.n_head), 256, 0, st>>>(a, part, mode, max_split, sm_count,
-                                                            nullptr, nullptr, m_out, l_out, o_out);
+  if (mode == 1)
+    decode_fast_combine<<<a.n_batch, 256, 0, st>>>(a, part, sm_count, nullptr, nullptr, m_out,
+                                                   l_out, o_out);
+  else
+    decode_combine<<<dim3(a.n_batch, a.n_head), 256, 0, st>>>(a, part, max_split, nullptr,
+                                                              nullptr, m_out, l_out, o_out);
   return cudaGetLastError();
 }
 
