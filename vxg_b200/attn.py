@@ -27,6 +27,16 @@ KvQ8Block = np.dtype([("d", "<u2"), ("qs", "i1", (32,))])
 assert KvQ8Block.itemsize == 34
 
 
+# cudaStreamLegacy: torch reports its default stream as handle 0, which the C ABI would read as
+# "no stream" (synchronous, on the context's own stream); name the legacy default stream instead.
+_CUDA_STREAM_LEGACY = 1
+
+
+def _stream_handle(s):
+    h = int(s.cuda_stream)
+    return ctypes.c_void_p(h if h != 0 else _CUDA_STREAM_LEGACY)
+
+
 def _is_torch(x) -> bool:
     return type(x).__module__.startswith("torch")
 
@@ -75,7 +85,7 @@ class _Args:
             return None
         import torch
         s = stream if stream is not None else torch.cuda.current_stream()
-        return ctypes.c_void_p(s.cuda_stream)
+        return _stream_handle(s)
 
 
 class Context:
@@ -113,12 +123,12 @@ class Context:
     def sync(self, stream=None) -> int:
         s = None
         if stream is not None:
-            s = ctypes.c_void_p(stream.cuda_stream)
+            s = _stream_handle(stream)
         else:
             try:
                 import torch
                 if torch.cuda.is_available():
-                    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+                    s = _stream_handle(torch.cuda.current_stream())
             except ImportError:
                 pass
         return check(lib().vxg_attn_cuda_sync(self.h, s, self._err.buf, self._err.cap), self._err)

@@ -150,7 +150,7 @@ constexpr uint32_t kWaitIters = 1u << 26;
 
 struct __align__(128) Smem {
   uint8_t stage[NS][2][STB];       // [buf][K, V][token][kv head][block] raw KvQ8Blocks
-  float wsc[WARPS][2][4][NB][4];   // per-warp K/V scales: [q][block][tokens 2q,2q+1,2q+8,2q+9]
+  float wsc[WARPS][2][NB][4][4];   // per-warp K/V scales: [block][q][tokens 2q,2q+1,2q+8,2q+9]
   int prefix[MAXB + 1];            // units before batch entry b
   unsigned done[NS];               // warps finished with each buffer
   uint64_t full[NS];
@@ -334,8 +334,8 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
   int b = find_batch(sm.prefix, B, u0);
   int seg_new = 1;
   int e_beg = 0, e_end = 0, e_seq = 0;
-  const float4* wsk = reinterpret_cast<const float4*>(&sm.wsc[warp][0][q][0][0]);
-  const float4* wsv = reinterpret_cast<const float4*>(&sm.wsc[warp][1][q][0][0]);
+  const float4* wsk = reinterpret_cast<const float4*>(&sm.wsc[warp][0][0][q][0]);  // + 4*c
+  const float4* wsv = reinterpret_cast<const float4*>(&sm.wsc[warp][1][0][q][0]);
   const int swk = g >> 2;   // K load order swizzle (bank conflicts between tokens g and g+4)
   const int swv = q >> 1;   // V load order swizzle (tokens 2q and 2q+4)
 
@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
                         ? f16bits_to_f32(*reinterpret_cast<const uint16_t*>(src + tok * TOKB + c * kBlk))
                         : 0.f;
           }
-          *reinterpret_cast<float4*>(&sm.wsc[warp][which][qq][c][0]) = d;
+          *reinterpret_cast<float4*>(&sm.wsc[warp][which][c][qq][0]) = d;
         }
       }
       __syncwarp();
@@ -440,7 +440,7 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
       const uint8_t* rec0 = kst + (16 * sub + g) * TOKB + kh * REC;
 #pragma unroll
       for (int c = 0; c < NB; ++c) {
-        const float4 dk = wsk[c];
+        const float4 dk = wsk[4 * c];
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const uint8_t* blk = rec0 + 8 * j * TOKB + c * kBlk;
@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
       const uint8_t* vr1 = vst + (16 * sub + 2 * q + 1 - swv) * TOKB + kh * REC;  // second
 #pragma unroll
       for (int c = 0; c < NB; ++c) {
-        const float4 dv = wsv[c];
+        const float4 dv = wsv[4 * c];
         const uint32_t pb0 = pack_f16x2(p[0][0] * dv.x, p[0][1] * dv.y);
         const uint32_t pb1 = pack_f16x2(p[1][0] * dv.z, p[1][1] * dv.w);
         uint32_t f0, f1, f8, f9;
@@ -617,8 +617,8 @@ __global__ void __launch_bounds__(256) decode_combine(DecodeArgs a, Partials par
   }
 }
 
-// Fast-path combine: one CTA per batch entry, thread = output dimension, all 16 heads.  CTA i
-// of the split pass owned units [i*U/n_cta, (i+1)*U/n_cta); for each such CTA meeting entry b,
+// Fast-path combine: grid (batch entry, 64-dim chunk); thread = (dim, 4-head quad).  CTA i of
+// the split pass owned units [i*U/n_cta, (i+1)*U/n_cta); for each such CTA meeting entry b,
 // slots (i + b)*SUBS + sub hold the partials of its 4 sub-tiles, o stored [dim][head].
 __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partials part, int n_cta,
                                                            const float* gate, float* out,
@@ -626,30 +626,34 @@ __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partial
                                                            float* o_out) {
   using namespace fast;
   constexpr int H = NKV * G;
-  const int b = blockIdx.x, d = threadIdx.x;
+  constexpr int MAXS = 256 * SUBS;  // partial slots merged per entry (CTAs meeting one entry)
+  constexpr int CH = 128;           // slots whose merge factors are staged at a time
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int d = blockIdx.y * 64 + (tid >> 2), hq = tid & 3;
   __shared__ long long red[2][256];
-  __shared__ int s_list[256];
+  __shared__ int s_slot[MAXS];
+  __shared__ float s_f[CH][H];
   __shared__ int s_n;
   __shared__ float s_M[H], s_L[H];
   const int len = entry_len(a, b);
-  if (d == 0 && !entry_valid(a, b)) atomicOr(a.status, kStatusBadIndex);
+  if (tid == 0 && blockIdx.y == 0 && !entry_valid(a, b)) atomicOr(a.status, kStatusBadIndex);
   long long before = 0, tot = 0;
-  for (int i = d; i < a.n_batch; i += 256) {
+  for (int i = tid; i < a.n_batch; i += 256) {
     const long long un = (entry_len(a, i) + ST - 1) / ST;
     tot += un;
     if (i < b) before += un;
   }
-  red[0][d] = before;
-  red[1][d] = tot;
+  red[0][tid] = before;
+  red[1][tid] = tot;
   __syncthreads();
   for (int st = 128; st > 0; st >>= 1) {
-    if (d < st) {
-      red[0][d] += red[0][d + st];
-      red[1][d] += red[1][d + st];
+    if (tid < st) {
+      red[0][tid] += red[0][tid + st];
+      red[1][tid] += red[1][tid + st];
     }
     __syncthreads();
   }
-  if (d == 0) {
+  if (tid == 0) {
     const long long U = red[1][0], P0 = red[0][0];
     const long long P1 = P0 + (len + ST - 1) / ST;
     int n = 0;
@@ -658,63 +662,63 @@ __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partial
       long long ihi = (P1 * n_cta + U - 1) / U - 1;
       if (ilo < 0) ilo = 0;
       if (ihi > n_cta - 1) ihi = n_cta - 1;
-      for (long long i = ilo; i <= ihi && n < 256; ++i) {
+      for (long long i = ilo; i <= ihi && n + SUBS <= MAXS; ++i) {
         const long long r0 = i * U / n_cta, r1 = (i + 1) * U / n_cta;
-        if (max(r0, P0) < min(r1, P1)) s_list[n++] = (int)(i + b);
+        if (max(r0, P0) < min(r1, P1))
+          for (int s2 = 0; s2 < SUBS; ++s2) s_slot[n++] = (int)((i + b) * SUBS + s2);
       }
     }
     s_n = n;
   }
   __syncthreads();
-  const int ns = s_n * SUBS;
-  if (d < H) {
+  const int ns = s_n;
+  if (tid < H) {
     float M = -INFINITY;
-    for (int k = 0; k < ns; ++k) {
-      const size_t sl = (size_t)s_list[k / SUBS] * SUBS + k % SUBS;
-      M = fmaxf(M, part.m[sl * H + d]);
-    }
-    float L = 0.f;
-    if (M != -INFINITY)
-      for (int k = 0; k < ns; ++k) {
-        const size_t sl = (size_t)s_list[k / SUBS] * SUBS + k % SUBS;
-        const float mk = part.m[sl * H + d];
-        if (mk != -INFINITY) L = fmaf(part.l[sl * H + d], exp2f(mk - M), L);
-      }
-    s_M[d] = M;
-    s_L[d] = L;
+    for (int k = 0; k < ns; ++k) M = fmaxf(M, part.m[(size_t)s_slot[k] * H + tid]);
+    s_M[tid] = M;
   }
   __syncthreads();
-  float acc[H];
-#pragma unroll
-  for (int h = 0; h < H; ++h) acc[h] = 0.f;
-  for (int k = 0; k < ns; ++k) {
-    const size_t sl = (size_t)s_list[k / SUBS] * SUBS + k % SUBS;
-    const float4* src = reinterpret_cast<const float4*>(part.o + (sl * HD + d) * H);
-#pragma unroll
-    for (int v = 0; v < H / 4; ++v) {
-      const float4 x = src[v];
-      const float* xp = &x.x;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int h = 4 * v + e;
-        const float mk = part.m[sl * H + h];
-        const float f = (mk == -INFINITY || s_M[h] == -INFINITY) ? 0.f : exp2f(mk - s_M[h]);
-        acc[h] = fmaf(xp[e], f, acc[h]);
-      }
+  // per (slot, head) merge factors, staged CH slots at a time; L per head
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float Lp = 0.f;
+  for (int k0 = 0; k0 < ns; k0 += CH) {
+    const int nk = min(CH, ns - k0);
+    for (int idx = tid; idx < nk * H; idx += 256) {
+      const int k = idx / H, h = idx % H;
+      const float mk = part.m[(size_t)s_slot[k0 + k] * H + h];
+      s_f[k][h] = (mk == -INFINITY || s_M[h] == -INFINITY) ? 0.f : exp2f(mk - s_M[h]);
     }
+    __syncthreads();
+    if (tid < H)
+      for (int k = 0; k < nk; ++k)
+        Lp = fmaf(part.l[(size_t)s_slot[k0 + k] * H + tid], s_f[k][tid], Lp);
+    for (int k = 0; k < nk; ++k) {
+      const float4 x = *reinterpret_cast<const float4*>(
+          part.o + ((size_t)s_slot[k0 + k] * HD + d) * H + 4 * hq);
+      const float* f = &s_f[k][4 * hq];
+      acc.x = fmaf(x.x, f[0], acc.x);
+      acc.y = fmaf(x.y, f[1], acc.y);
+      acc.z = fmaf(x.z, f[2], acc.z);
+      acc.w = fmaf(x.w, f[3], acc.w);
+    }
+    __syncthreads();
   }
+  if (tid < H) s_L[tid] = Lp;
+  __syncthreads();
+  const float* ap = &acc.x;
 #pragma unroll
-  for (int h = 0; h < H; ++h) {
+  for (int e = 0; e < 4; ++e) {
+    const int h = 4 * hq + e;
     const size_t oi = ((size_t)b * H + h) * HD + d;
     if (m_out) {
-      o_out[oi] = acc[h];
+      o_out[oi] = ap[e];
       if (d == 0) {
         m_out[(size_t)b * H + h] = s_M[h];
         l_out[(size_t)b * H + h] = s_L[h];
       }
     } else {
       const float L = s_L[h];
-      float r = (L > 0.f || L != L) ? acc[h] / L : 0.f;  // NaN partials stay NaN
+      float r = (L > 0.f || L != L) ? ap[e] / L : 0.f;  // NaN partials stay NaN
       if (gate) r *= 1.0f / (1.0f + expf(-gate[oi]));
       if (!isfinite(r)) atomicOr(a.status, kStatusNonFinite);
       out[oi] = r;
@@ -828,8 +832,8 @@ cudaError_t launch_decode(const DecodeArgs& a, const Partials& part, const float
   if (e != cudaSuccess) return e;
   if (ev1) cudaEventRecord(ev1, st);
   if (mode == 1)
-    decode_fast_combine<<<a.n_batch, 256, 0, st>>>(a, part, sm_count, gate, out, nullptr,
-                                                   nullptr, nullptr);
+    decode_fast_combine<<<dim3(a.n_batch, fast::HD / 64), 256, 0, st>>>(
+        a, part, sm_count, gate, out, nullptr, nullptr, nullptr);
   else
     decode_combine<<<dim3(a.n_batch, a.n_head), 256, 0, st>>>(a, part, max_split, gate, out,
                                                               nullptr, nullptr, nullptr);
@@ -844,8 +848,8 @@ cudaError_t launch_decode_partial(const DecodeArgs& a, const Partials& part, flo
   cudaError_t e = run_split(a, part, sm_count, force_generic, st, &mode, &max_split);
   if (e != cudaSuccess) return e;
   if (mode == 1)
-    decode_fast_combine<<<a.n_batch, 256, 0, st>>>(a, part, sm_count, nullptr, nullptr, m_out,
-                                                   l_out, o_out);
+    decode_fast_combine<<<dim3(a.n_batch, fast::HD / 64), 256, 0, st>>>(
+        a, part, sm_count, nullptr, nullptr, m_out, l_out, o_out);
   else
     decode_combine<<<dim3(a.n_batch, a.n_head), 256, 0, st>>>(a, part, max_split, nullptr,
                                                               nullptr, m_out, l_out, o_out);
