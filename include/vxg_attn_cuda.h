@@ -131,6 +131,25 @@ VXG_ATTN_API int vxg_attn_cuda_q8_decode(void* ctx, void* kv, uint32_t n_batch, 
                             float scale, uint32_t max_ctx, float* out, int memkind, void* stream,
                             char* err, size_t cap);
 
+/* The same decode step as vxg_attn_cuda_q8_decode for callers that cannot allocate device
+ * memory.  This entry point has no counterpart in the reference.  It is for engines whose device
+ * memory belongs to a budgeted pool or to another framework's allocator, and for decode loops
+ * that must not stall on cudaMalloc, which can synchronise the device.  It allocates nothing:
+ * every argument is caller-owned device memory, the KV pools included (layout as above, e.g.
+ * from vxg_attn_cuda_kv_device_ptrs or the caller's own buffers), and its split-KV scratch is a
+ * built-in 16 MiB device array that each GPU using the library keeps until the process exits.
+ * A batch whose scratch does not fit is rejected with VXG_ATTN_ERR_BUFFER_TOO_SMALL (at 16 q /
+ * 2 kv heads, head_dim 256 on a 148-SM B200: up to 106 entries per call).  All calls on a device
+ * share that array, so calls that overlap on the GPU race; serialise them.  The first call on a
+ * device sets up the array's address for that device; make it before any stream capture.  With
+ * stream == NULL the call runs on the default stream and reports the device status like
+ * vxg_attn_cuda_q8_decode; with a stream it is asynchronous and reports launch errors only. */
+VXG_ATTN_API int vxg_attn_cuda_q8_decode_noalloc(
+    void* k_pool, void* v_pool, uint32_t n_seq, uint32_t cap_tokens, uint32_t n_head_kv,
+    uint32_t head_dim, uint32_t n_batch, uint32_t n_head, const int32_t* seq_ids,
+    const int32_t* pos, const float* q, const float* k_new, const float* v_new,
+    const float* q_gate, float scale, float* out, void* stream, char* err, size_t cap);
+
 /* Split-KV partial over tokens [kv_begin[b], kv_end[b]) of each sequence (no append): per
  * (b, head) the running max m (log2 units: max_t score_t * log2(e)), the sum
  * l = sum_t 2^(score_t*log2(e) - m) and the unnormalised o = sum_t 2^(...) * v_t.  Shapes:
