@@ -336,8 +336,11 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
   int e_beg = 0, e_end = 0, e_seq = 0;
   const float4* wsk = reinterpret_cast<const float4*>(&sm.wsc[warp][0][0][q][0]);  // + 4*c
   const float4* wsv = reinterpret_cast<const float4*>(&sm.wsc[warp][1][0][q][0]);
-  const int swk = g >> 2;   // K load order swizzle (bank conflicts between tokens g and g+4)
-  const int swv = q >> 1;   // V load order swizzle (tokens 2q and 2q+4)
+  // Inside each 8-token n-tile, MMA column n holds token (n >> 1) + 4 * (n & 1): the V loads of
+  // lane (g, q) then read tokens q and 4 + q, whose 544-B rows start in different banks, and
+  // the K loads only need their word order swapped on odd columns (swk) to avoid conflicts.
+  const int swk = g & 1;
+  const int tok_k = (g >> 1) + 4 * (g & 1);  // token loaded for K column g
 
   for (int u = u0; u < u1; ++u) {
     const int it = u - u0;
@@ -426,7 +429,7 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
           float* dp = &d.x;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int tok = 16 * sub + 2 * qq + (i & 1) + 8 * (i >> 1);
+            const int tok = 16 * sub + qq + 4 * (i & 1) + 8 * (i >> 1);
             dp[i] = tok < ntok
                         ? f16bits_to_f32(*reinterpret_cast<const uint16_t*>(src + tok * TOKB + c * kBlk))
                         : 0.f;
@@ -437,7 +440,7 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
       __syncwarp();
       // ---- S = Q K^T on int8 tensor cores: 2 n-tiles of 8 tokens ---------------------------
       float sacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-      const uint8_t* rec0 = kst + (16 * sub + g) * TOKB + kh * REC;
+      const uint8_t* rec0 = kst + (16 * sub + tok_k) * TOKB + kh * REC;
 #pragma unroll
       for (int c = 0; c < NB; ++c) {
         const float4 dk = wsk[4 * c];
@@ -468,7 +471,7 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
       for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int tl = 16 * sub + 8 * j + 2 * q + e;
+          const int tl = 16 * sub + 8 * j + q + 4 * e;
           p[j][e] = tl < ntok ? sacc[j][e] * fac : -INFINITY;
           mx = fmaxf(mx, p[j][e]);
         }
@@ -503,8 +506,8 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
           }
       }
       // ---- O^T += V^T P'^T on f16 tensor cores, P' = p * d_v ---------------------------------
-      const uint8_t* vr0 = vst + (16 * sub + 2 * q + swv) * TOKB + kh * REC;      // first
-      const uint8_t* vr1 = vst + (16 * sub + 2 * q + 1 - swv) * TOKB + kh * REC;  // second
+      const uint8_t* vr0 = vst + (16 * sub + q) * TOKB + kh * REC;      // column 2q
+      const uint8_t* vr1 = vst + (16 * sub + 4 + q) * TOKB + kh * REC;  // column 2q + 1
 #pragma unroll
       for (int c = 0; c < NB; ++c) {
         const float4 dv = wsv[4 * c];
@@ -522,8 +525,8 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
           f8 = load_group<0>(vr0 + 8 * TOKB + c * kBlk, g);
           f9 = load_group<0>(vr1 + 8 * TOKB + c * kBlk, g);
         }
-        const uint32_t w0 = (swv ? f1 : f0) ^ 0x80808080u, w1 = (swv ? f0 : f1) ^ 0x80808080u;
-        const uint32_t w8 = (swv ? f9 : f8) ^ 0x80808080u, w9 = (swv ? f8 : f9) ^ 0x80808080u;
+        const uint32_t w0 = f0 ^ 0x80808080u, w1 = f1 ^ 0x80808080u;
+        const uint32_t w8 = f8 ^ 0x80808080u, w9 = f9 ^ 0x80808080u;
         const uint32_t lo01 = prmt(w0, w1, 0x5140), lo23 = prmt(w0, w1, 0x7362);
         const uint32_t hi01 = prmt(w8, w9, 0x5140), hi23 = prmt(w8, w9, 0x7362);
         hmma_16816(o[c][0], codes_to_f16x2(lo01, 0x4140), codes_to_f16x2(lo01, 0x4342),
@@ -633,6 +636,8 @@ __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partial
   __shared__ long long red[2][256];
   __shared__ int s_slot[MAXS];
   __shared__ float s_f[CH][H];
+  __shared__ float s_l[CH][H];
+  __shared__ float s_Mnew[H];
   __shared__ int s_n;
   __shared__ float s_M[H], s_L[H];
   const int len = entry_len(a, b);
@@ -672,26 +677,55 @@ __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partial
   }
   __syncthreads();
   const int ns = s_n;
-  if (tid < H) {
-    float M = -INFINITY;
-    for (int k = 0; k < ns; ++k) M = fmaxf(M, part.m[(size_t)s_slot[k] * H + tid]);
-    s_M[tid] = M;
-  }
-  __syncthreads();
-  // per (slot, head) merge factors, staged CH slots at a time; L per head
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float Lp = 0.f;
+  // Slots are processed CH at a time: their m and l are staged in shared memory by all threads
+  // (independent loads), the running max per head is kept, and the accumulators are rescaled
+  // when it grows -- an online log-sum-exp over the slots.
+  float Mrun = -INFINITY;  // per head (threads < H), and per quad head via s_M
+  if (tid < H) s_M[tid] = -INFINITY;
   for (int k0 = 0; k0 < ns; k0 += CH) {
     const int nk = min(CH, ns - k0);
     for (int idx = tid; idx < nk * H; idx += 256) {
       const int k = idx / H, h = idx % H;
-      const float mk = part.m[(size_t)s_slot[k0 + k] * H + h];
-      s_f[k][h] = (mk == -INFINITY || s_M[h] == -INFINITY) ? 0.f : exp2f(mk - s_M[h]);
+      s_f[k][h] = part.m[(size_t)s_slot[k0 + k] * H + h];
+      s_l[k][h] = part.l[(size_t)s_slot[k0 + k] * H + h];
     }
     __syncthreads();
-    if (tid < H)
-      for (int k = 0; k < nk; ++k)
-        Lp = fmaf(part.l[(size_t)s_slot[k0 + k] * H + tid], s_f[k][tid], Lp);
+    if (tid < H) {
+      float M = Mrun;
+      for (int k = 0; k < nk; ++k) M = fmaxf(M, s_f[k][tid]);
+      s_Mnew[tid] = M;
+    }
+    __syncthreads();
+    // rescale what was accumulated so far, then turn the staged m into merge factors
+    float sc[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float mo = s_M[4 * hq + e], mn = s_Mnew[4 * hq + e];
+      sc[e] = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
+    }
+    acc.x *= sc[0];
+    acc.y *= sc[1];
+    acc.z *= sc[2];
+    acc.w *= sc[3];
+    if (tid < H) {
+      const float mo = s_M[tid], mn = s_Mnew[tid];
+      Lp *= (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
+      Mrun = mn;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < nk * H; idx += 256) {
+      const int k = idx / H, h = idx % H;
+      const float mk = s_f[k][h], mn = s_Mnew[h];
+      s_f[k][h] = (mk == -INFINITY || mn == -INFINITY) ? 0.f : exp2f(mk - mn);
+    }
+    __syncthreads();
+    if (tid < H) {
+      s_M[tid] = Mrun;
+      for (int k = 0; k < nk; ++k) Lp = fmaf(s_l[k][tid], s_f[k][tid], Lp);
+    }
+#pragma unroll 4
     for (int k = 0; k < nk; ++k) {
       const float4 x = *reinterpret_cast<const float4*>(
           part.o + ((size_t)s_slot[k0 + k] * HD + d) * H + 4 * hq);
