@@ -139,12 +139,12 @@ constexpr int G = 8;               // query heads per kv head
 constexpr int NKV = 2;             // kv heads (both handled by every CTA)
 constexpr int REC = NB * kBlk;     // 272 B per (token, kv head)
 constexpr int TOKB = NKV * REC;    // 544 B per token in one cache
-constexpr int ST = 64;             // tokens per unit / stage
-constexpr int NS = 3;              // stages in flight
+constexpr int ST = 96;             // tokens per unit / stage
+constexpr int NS = 2;              // stages in flight
 constexpr int STB = ST * TOKB;     // 34816 B per stage per cache
-constexpr int WARPS = 8;           // (kv head, 16-token sub-tile)
+constexpr int WARPS = 12;          // (kv head, 16-token sub-tile)
 constexpr int THREADS = WARPS * 32;
-constexpr int SUBS = 4;            // 16-token sub-tiles per stage = partial slots per segment
+constexpr int SUBS = 6;            // 16-token sub-tiles per stage = partial slots per segment
 constexpr int MAXB = 1024;         // batch entries per launch
 constexpr uint32_t kWaitIters = 1u << 26;
 
