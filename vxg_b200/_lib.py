@@ -9,7 +9,8 @@ import os
 import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libvxg_attn_cuda.so")
+# VXG_ATTN_LIB selects another build of the same library (A/B comparisons of builds).
+LIB_PATH = os.environ.get("VXG_ATTN_LIB") or os.path.join(HERE, "libvxg_attn_cuda.so")
 
 OK = 0
 WARN_NONFINITE = 1

@@ -46,10 +46,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                "r"(bytes)
                : "memory");
 }
-// Bounded wait on phase `parity`.  Returns false if it gave up after `max_iter` polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t max_iter) {
-  uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < max_iter; ++i) {
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for the completion of the phase of `bar` with parity `parity`, for at most timeout_ns of
+// wall-clock time.  Returns false if it gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+  const uint32_t addr = smem_u32(bar);
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
@@ -58,8 +65,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((i & 1023u) == 0) {  // the timer is read rarely: polls stay cheap
+      const uint64_t t = globaltimer_ns();
+      if (i == 0) t0 = t;
+      else if (t - t0 > timeout_ns) return false;
+    }
   }
-  return false;
 }
 // global -> shared bulk copy completing on `bar` (bytes and both addresses multiples of 16).
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,

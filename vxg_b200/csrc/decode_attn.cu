@@ -141,19 +141,24 @@ constexpr int REC = NB * kBlk;     // 272 B per (token, kv head)
 constexpr int TOKB = NKV * REC;    // 544 B per token in one cache
 constexpr int ST = 96;             // tokens per unit / stage
 constexpr int NS = 2;              // stages in flight
-constexpr int STB = ST * TOKB;     // 34816 B per stage per cache
-constexpr int WARPS = 12;          // (kv head, 16-token sub-tile)
+constexpr int STB = ST * TOKB;     // bytes per stage per cache (52224 at ST = 96)
+constexpr int SPK = ST / 16;       // 16-token sub-tiles per kv head in a stage
+constexpr int WPS = NKV * SPK;     // warps working on one stage
+constexpr int GROUPS = 1;          // warp groups taking alternate stages (1: all warps, every stage)
+constexpr int WARPS = WPS * GROUPS;
 constexpr int THREADS = WARPS * 32;
-constexpr int SUBS = 6;            // 16-token sub-tiles per stage = partial slots per segment
+constexpr int SUBS = SPK * GROUPS; // partial slots per (CTA, batch entry) per kv head
 constexpr int MAXB = 1024;         // batch entries per launch
-constexpr uint32_t kWaitIters = 1u << 26;
+constexpr uint64_t kWaitNs = 2000000000ull;  // give up a stage wait after 2 s
+constexpr int NBAR = 2 * NS;       // stage barriers: stage it uses barrier it % NBAR, so each
+                                   // barrier serves only one warp group (NBAR even)
 
 struct __align__(128) Smem {
   uint8_t stage[NS][2][STB];       // [buf][K, V][token][kv head][block] raw KvQ8Blocks
   float wsc[WARPS][2][NB][4][4];   // per-warp K/V scales: [block][q][tokens 2q,2q+1,2q+8,2q+9]
   int prefix[MAXB + 1];            // units before batch entry b
   unsigned done[NS];               // warps finished with each buffer
-  uint64_t full[NS];
+  uint64_t full[NBAR];
 };
 }  // namespace fast
 
@@ -275,7 +280,8 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
-  const int kh = warp & 1, sub = warp >> 1;
+  const int kh = warp & 1, sub = (warp >> 1) % SPK, grp = warp / WPS;
+  const int slot_sub = warp >> 1;  // grp * SPK + sub
   const int B = a.n_batch;
 
   // ---- unit prefix over the batch (warp 0: serial per lane chunk + warp scan) -----------
@@ -303,10 +309,8 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
     if (lane == 31) sm.prefix[B] = incl;
   }
   if (tid == 0) {
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&sm.full[i], 1);
-      sm.done[i] = 0;
-    }
+    for (int i = 0; i < NBAR; ++i) mbar_init(&sm.full[i], 1);
+    for (int i = 0; i < NS; ++i) sm.done[i] = 0;
     fence_mbar_init();
   }
   __syncthreads();
@@ -315,25 +319,56 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
   const int u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
   if (u0 >= u1) return;
 
-  auto issue = [&](int u, int buf) {
+  auto issue = [&](int u) {  // unit u -> buffer (u - u0) % NS, barrier (u - u0) % NBAR
     const UnitInfo ui = unit_info(a, sm.prefix, u);
     const uint32_t bytes = (uint32_t)ui.ntok * TOKB;
     const size_t off = ((size_t)ui.s * a.cap + ui.t_start) * TOKB;
-    mbar_arrive_expect_tx(&sm.full[buf], 2 * bytes);
-    bulk_g2s(sm.stage[buf][0], a.k_pool + off, bytes, &sm.full[buf]);
-    bulk_g2s(sm.stage[buf][1], a.v_pool + off, bytes, &sm.full[buf]);
+    const int buf = (u - u0) % NS;
+    uint64_t* bar = &sm.full[(u - u0) % NBAR];
+    mbar_arrive_expect_tx(bar, 2 * bytes);
+    bulk_g2s(sm.stage[buf][0], a.k_pool + off, bytes, bar);
+    bulk_g2s(sm.stage[buf][1], a.v_pool + off, bytes, bar);
   };
   if (tid == 0)
-    for (int i = 0; i < NS && u0 + i < u1; ++i) issue(u0 + i, i);
+    for (int i = 0; i < NS && u0 + i < u1; ++i) issue(u0 + i);
 
   uint32_t qa[NB][4];      // int8 digit fragments of this warp's 8 query heads
   float fac = 0.f;         // per-head factor sigma/254 * scale * log2(e) (head g)
   float o[NB][2][4];       // O^T accumulators: [block][m-tile][frag]
   float m_run = -INFINITY, l_run = 0.f;
-  // current batch entry (incremental walk over the units)
-  int b = find_batch(sm.prefix, B, u0);
-  int seg_new = 1;
-  int e_beg = 0, e_end = 0, e_seq = 0;
+  // Entry walk: this warp takes units u0 + grp, u0 + grp + GROUPS, ...  It owes a partial for
+  // every batch entry with units in [u0, u1); entries whose units here all belong to the other
+  // group get an empty partial (m = -inf, l = 0, o = 0).
+  int b = -1;                                   // entry of the live accumulators
+  int e_next = find_batch(sm.prefix, B, u0);    // first entry still owed
+  int e_beg = 0, e_end = 0;
+  auto write_partial = [&](int e, bool empty) {
+    const size_t slot = ((size_t)blockIdx.x + e) * SUBS + slot_sub;
+    float lt = empty ? 0.f : l_run;
+    lt += __shfl_xor_sync(0xffffffffu, lt, 1);
+    lt += __shfl_xor_sync(0xffffffffu, lt, 2);
+    if (q == 0) {
+      part.m[slot * a.n_head + kh * G + g] = empty ? -INFINITY : m_run;
+      part.l[slot * a.n_head + kh * G + g] = lt;
+    }
+    float* po = part.o + slot * a.n_head * HD + kh * G + 2 * q;   // [dim][head]
+#pragma unroll
+    for (int c = 0; c < NB; ++c)
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int dim = group_dim(c, g, 2 * mt + r);
+          *reinterpret_cast<float2*>(po + (size_t)dim * a.n_head) =
+              empty ? make_float2(0.f, 0.f) : make_float2(o[c][mt][2 * r], o[c][mt][2 * r + 1]);
+        }
+  };
+  auto owe_empty_until = [&](int e_stop) {     // empty partials for entries [e_next, e_stop)
+    if constexpr (GROUPS > 1) {  // with one group every warp sees every unit: nothing owed
+      for (; e_next < e_stop; ++e_next)
+        if (sm.prefix[e_next + 1] > sm.prefix[e_next]) write_partial(e_next, true);
+    }
+  };
   const float4* wsk = reinterpret_cast<const float4*>(&sm.wsc[warp][0][0][q][0]);  // + 4*c
   const float4* wsv = reinterpret_cast<const float4*>(&sm.wsc[warp][1][0][q][0]);
   // Inside each 8-token n-tile, MMA column n holds token (n >> 1) + 4 * (n & 1): the V loads of
@@ -342,17 +377,17 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
   const int swk = g & 1;
   const int tok_k = (g >> 1) + 4 * (g & 1);  // token loaded for K column g
 
-  for (int u = u0; u < u1; ++u) {
+  for (int u = u0 + grp; u < u1; u += GROUPS) {
     const int it = u - u0;
     const int buf = it % NS;
-    const uint32_t par = (uint32_t)(it / NS) & 1u;
-    while (u >= sm.prefix[b + 1]) {
-      ++b;
-      seg_new = 1;
-    }
-    if (seg_new) {
-      seg_new = 0;
-      e_seq = a.seq_ids[b];
+    const int bar = it % NBAR;
+    const uint32_t par = (uint32_t)(it / NBAR) & 1u;
+    int bu = b < 0 ? e_next : b;
+    while (u >= sm.prefix[bu + 1]) ++bu;
+    if (bu != b) {
+      owe_empty_until(bu);
+      e_next = bu + 1;
+      b = bu;
       e_beg = a.kv_begin ? a.kv_begin[b] : 0;
       e_end = a.kv_end[b] + a.end_add;
       // ---- query digits: q ~= sigma * (d_a + d_b / 254), sigma = max|q| / 127 ------------
@@ -407,11 +442,11 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
     const int ntok = min(ST, e_end - t_start);
 
     // ---- wait for this stage (bounded, per warp) -------------------------------------------
-    if (!mbar_wait(&sm.full[buf], par, kWaitIters)) {
+    if (!mbar_wait(&sm.full[bar], par, kWaitNs)) {
       // Give up: flag it, let the copies this CTA issued land (bounded), then leave.
       if (lane == 0) atomicOr(a.status, kStatusTimeout);
       for (int k = 1; k < NS; ++k)
-        if (u + k < u1) mbar_wait(&sm.full[(it + k) % NS], (uint32_t)((it + k) / NS) & 1u, kWaitIters);
+        if (u + k < u1) mbar_wait(&sm.full[(it + k) % NBAR], (uint32_t)((it + k) / NBAR) & 1u, kWaitNs);
       return;
     }
     const uint8_t* kst = sm.stage[buf][0];
@@ -541,40 +576,20 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
     if (lane == 0) {
       __threadfence_block();
       const unsigned prev = atomicAdd(&sm.done[buf], 1u);
-      if (prev == WARPS - 1) {
+      if (prev == WPS - 1) {
         sm.done[buf] = 0;
         __threadfence_block();
         if (u + NS < u1) {
           fence_proxy_async_smem();
-          issue(u + NS, buf);
+          issue(u + NS);
         }
       }
     }
 
-    // ---- end of this (batch entry, CTA) segment: write this warp's partial -----------------
-    if (u + 1 == u1 || u + 1 >= sm.prefix[b + 1]) {
-      const size_t slot = ((size_t)blockIdx.x + b) * SUBS + sub;
-      float lt = l_run;
-      lt += __shfl_xor_sync(0xffffffffu, lt, 1);
-      lt += __shfl_xor_sync(0xffffffffu, lt, 2);
-      if (q == 0) {
-        part.m[slot * a.n_head + kh * G + g] = m_run;
-        part.l[slot * a.n_head + kh * G + g] = lt;
-      }
-      float* po = part.o + slot * a.n_head * HD + kh * G + 2 * q;   // [dim][head]
-#pragma unroll
-      for (int c = 0; c < NB; ++c)
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            const int dim = group_dim(c, g, 2 * mt + r);
-            *reinterpret_cast<float2*>(po + (size_t)dim * a.n_head) =
-                make_float2(o[c][mt][2 * r], o[c][mt][2 * r + 1]);
-          }
-      seg_new = 1;
-    }
+    // ---- this warp's last unit of the entry in this CTA: write its partial -----------------
+    if (u + GROUPS >= u1 || u + GROUPS >= sm.prefix[b + 1]) write_partial(b, false);
   }
+  if constexpr (GROUPS > 1) owe_empty_until(find_batch(sm.prefix, B, u1 - 1) + 1);
 }
 
 // =============================================================================================
