@@ -349,7 +349,9 @@ def run_deltanet(args, world, rank, local):
 
 
 def run_long(args, world, rank, local):
-    """BASELINE config 3 on one GPU: B=1, ctx 262144, 1% of K rows x8, split-KV across SMs."""
+    """B=1, ctx 262144, 1% of K rows x8.  One GPU: split-KV across its SMs.
+    N GPUs: the KV range is split across ranks (vxg_b200.dist.LongContextDecoder): append on the
+    owning rank, per-rank split-KV partial, NCCL all-gather of (m, l, o), LSE combine."""
     import torch
     import torch.distributed as dist
     import vxg_b200
@@ -358,37 +360,51 @@ def run_long(args, world, rank, local):
     ctx = vxg_b200.Context()
     L = 262144
     cap = L + W + K + 8
-    pool = vxg_b200.KvQ8Pool(ctx, 1, wl.HKV, wl.HD, cap)
-    wl.fill_pool_device(pool, [L], seed=3, outlier_frac=0.01)
     q, kn, vn = wl.decode_step_inputs_device(1, W + K, seed=4)
-    seq = torch.zeros(1, dtype=torch.int32, device="cuda")
-    pos = [torch.tensor([L + i], dtype=torch.int32, device="cuda") for i in range(W + K)]
-    out = torch.empty((1, wl.HQ, wl.HD), device="cuda")
-    for i in range(W):
-        pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=out, max_ctx=cap)
-    ctx.sync()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    if world == 1:
+        pool = vxg_b200.KvQ8Pool(ctx, 1, wl.HKV, wl.HD, cap)
+        wl.fill_pool_device(pool, [L], seed=3, outlier_frac=0.01)
+        seq = torch.zeros(1, dtype=torch.int32, device="cuda")
+        pos = [torch.tensor([L + i], dtype=torch.int32, device="cuda") for i in range(W + K)]
+        out = torch.empty((1, wl.HQ, wl.HD), device="cuda")
+        step = lambda i: pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=out, max_ctx=cap)
+    else:
+        from vxg_b200.dist import LongContextDecoder
+        dec = LongContextDecoder(ctx, cap, wl.HQ, wl.HKV, wl.HD, world, rank)
+        mine = dec.range.local_len(L)
+        wl.fill_pool_device(dec.pool, [mine], seed=3 + rank, outlier_frac=0.01)
+        step = lambda i: dec.step(L + i, q[i], kn[i], vn[i])
+    for i in range(W):
+        step(i)
+    ctx.sync()
     barrier(torch, dist, world)
+    sampler = ClockSampler(local)
     ctx.set_timing(True)
+    sampler.start()
     e0.record()
     for i in range(W, W + K):
-        pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=out, max_ctx=cap)
+        step(i)
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    split = ctx.split_ms_total() / K
-    alg = (L + W + K / 2) * wl.TOKEN_BYTES
+    sampler.stop()
+    ms = barrier_max(torch, dist, world, e0.elapsed_time(e1))
+    split = barrier_max(torch, dist, world, ctx.split_ms_total() / K)
+    alg = (L + W + K / 2) * wl.TOKEN_BYTES / world
     peak, peak_kind = measured_peaks()
     ach = alg / (split * 1e-3) / 1e9
     return {"metric": METRIC, "value": K / (ms * 1e-3), "unit": "seq-steps/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config3: B=1 ctx 262144, 1% K rows x8, split-KV over SMs"},
+            "config": {"workload": "config3: B=1 ctx 262144, 1% K rows x8, split-KV over SMs"
+                                   + (f" and {world} GPUs (NCCL all-gather + LSE combine)"
+                                      if world > 1 else ""),
+                       "l2": "inputs larger than L2 (285 MB of KV per step)"},
             "roofline": {"kernel": "decode_fast_split", "bound": "hbm", "achieved": ach,
                          "peak": peak, "unit": "GB/s", "frac": ach / peak,
                          "peak_kind": peak_kind, "split_ms_per_launch": split},
-            "gpu_launches": 3 * K}
+            "gpu_launches": (3 if world == 1 else 4) * K, "clocks": sampler.summary()}
 
 
 # --------------------------------------------------------------------------- reference arm

@@ -191,6 +191,31 @@ VXG_ATTN_API int vxg_attn_cuda_deltanet_step(void* ctx, uint32_t n_batch, uint32
                                 float* state, float* o, int memkind, void* stream, char* err,
                                 size_t cap);
 
+/* Gated-DeltaNet core over n_tok consecutive tokens of each sequence (prefill).  The reference
+ * prefill applies the recurrent step token by token (llm_prefill.rs:470-480 calling
+ * llm_ops.rs:103-193); this runs the same recurrence with the state kept on chip.  q, k
+ * [n_batch][n_tok][n_kh][dk], v [n_batch][n_tok][n_vh][dv], beta_raw / alpha_raw
+ * [n_batch][n_tok][n_vh]; state [n_batch][n_vh][dv][dk] updated in place; o
+ * [n_batch][n_tok][n_vh][dv] = S_t q_t for every token. */
+VXG_ATTN_API int vxg_attn_cuda_deltanet_prefill(
+    void* ctx, uint32_t n_batch, uint32_t n_tok, uint32_t n_kh, uint32_t n_vh, uint32_t dk,
+    uint32_t dv, const float* q, const float* k, const float* v, const float* beta_raw,
+    const float* alpha_raw, const float* ssm_a, const float* dt_bias, float q_scale, float eps,
+    float* state, float* o, int memkind, void* stream, char* err, size_t cap);
+
+/* Drop-in for step_deltanet_recurrent (llm_ops.rs:103-121), batched over n_batch sequences:
+ * qkv_mixed [n_batch][conv_ch] (conv_ch = 2*n_kh*dk + n_vh*dv), z [n_batch][n_vh*dv],
+ * alpha_raw / beta_raw [n_batch][n_vh], ssm_conv1d [conv_ch][k_sz], ssm_a / ssm_dt_bias [n_vh],
+ * ssm_norm [dv]; conv_state [n_batch][k_sz-1][conv_ch] and ssm_state [n_batch][n_vh][dv][dk]
+ * are updated in place as in the reference; y_concat [n_batch][n_vh*dv] receives
+ * RMSNorm(S q) * ssm_norm * SiLU(z).  dk in {64,128,256}, dv a multiple of 32 up to 256. */
+VXG_ATTN_API int vxg_attn_cuda_step_deltanet_recurrent(
+    void* ctx, uint32_t n_batch, const float* qkv_mixed, uint32_t conv_ch, const float* z,
+    const float* alpha_raw, const float* beta_raw, const float* ssm_conv1d, const float* ssm_a,
+    const float* ssm_dt_bias, const float* ssm_norm, float* conv_state, float* ssm_state,
+    uint32_t n_kh, uint32_t n_vh, uint32_t dk, uint32_t dv, uint32_t k_sz, float eps,
+    float* y_concat, int memkind, void* stream, char* err, size_t cap);
+
 #ifdef __cplusplus
 }
 #endif

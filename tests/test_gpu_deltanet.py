@@ -69,3 +69,86 @@ def test_deltanet_rejects_bad_shapes(ctx):
         vxg_b200.deltanet_step(ctx, q, k, v, br, ar, np.ones(4, np.float32),
                                np.zeros(4, np.float32), state)
     assert e.value.code == -6
+
+
+def seq_inputs(rng, B, T, n_kh, n_vh, dk, dv):
+    q = rng.standard_normal((B, T, n_kh, dk)).astype(np.float32)
+    k = rng.standard_normal((B, T, n_kh, dk)).astype(np.float32)
+    v = rng.standard_normal((B, T, n_vh, dv)).astype(np.float32)
+    br = rng.standard_normal((B, T, n_vh)).astype(np.float32)
+    ar = rng.standard_normal((B, T, n_vh)).astype(np.float32)
+    return q, k, v, br, ar
+
+
+@pytest.mark.parametrize("B,T,n_kh,n_vh,dk,dv", [
+    (2, 96, 4, 8, 128, 128),
+    (3, 40, 2, 4, 64, 64),
+    (1, 33, 2, 2, 256, 96),
+])
+def test_deltanet_prefill_matches_token_by_token_oracle(ctx, B, T, n_kh, n_vh, dk, dv):
+    """The reference prefill applies the step token by token (llm_prefill.rs:470-480)."""
+    rng = np.random.default_rng(33)
+    state = (rng.standard_normal((B, n_vh, dv, dk)) * 0.02).astype(np.float32)
+    ref = state.copy()
+    A = -np.exp(rng.standard_normal(n_vh) * 0.3).astype(np.float32)
+    dt = (rng.standard_normal(n_vh) * 0.1).astype(np.float32)
+    q, k, v, br, ar = seq_inputs(rng, B, T, n_kh, n_vh, dk, dv)
+    o = vxg_b200.deltanet_prefill(ctx, q, k, v, br, ar, A, dt, state)
+    for t in range(T):
+        ro = oracle.batch_deltanet(q[:, t], k[:, t], v[:, t], br[:, t], ar[:, t], A, dt, n_kh,
+                                   n_vh, dk, dv, 1e-6, 1 / np.sqrt(dk), ref, n_threads=8)
+        np.testing.assert_allclose(o[:, t], ro, atol=ATOL, rtol=RTOL, err_msg=f"token {t}")
+    np.testing.assert_allclose(state, ref, atol=ATOL, rtol=RTOL)
+
+
+def test_deltanet_prefill_equals_decode_steps_long(ctx):
+    """Config-5b-like length: the on-chip recurrence over 2048 tokens equals 2048 decode steps
+    (both on the GPU; size-independent property)."""
+    import torch
+    rng = np.random.default_rng(34)
+    B, T, H, D = 2, 2048, 8, 128
+    q, k, v, br, ar = [torch.from_numpy(x).cuda() for x in seq_inputs(rng, B, T, H, H, D, D)]
+    s0 = torch.from_numpy((rng.standard_normal((B, H, D, D)) * 0.02).astype(np.float32)).cuda()
+    A = -torch.ones(H, device="cuda")
+    dt = torch.zeros(H, device="cuda")
+    s1 = s0.clone()
+    o1 = vxg_b200.deltanet_prefill(ctx, q, k, v, br, ar, A, dt, s1)
+    s2 = s0.clone()
+    o2 = torch.empty_like(o1)
+    for t in range(T):
+        o2[:, t] = vxg_b200.deltanet_step(ctx, q[:, t].contiguous(), k[:, t].contiguous(),
+                                          v[:, t].contiguous(), br[:, t].contiguous(),
+                                          ar[:, t].contiguous(), A, dt, s2)
+    ctx.sync()
+    torch.testing.assert_close(o1, o2, atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(s1, s2, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("n_kh,n_vh,dk,dv,k_sz", [(2, 4, 128, 128, 4), (1, 2, 64, 32, 3)])
+def test_step_deltanet_recurrent_dropin(ctx, n_kh, n_vh, dk, dv, k_sz):
+    """The whole reference step (conv1d + SiLU, core, RMSNorm * SiLU(z)) for several tokens."""
+    rng = np.random.default_rng(35)
+    B = 3
+    conv_ch = 2 * n_kh * dk + n_vh * dv
+    w = (rng.standard_normal((conv_ch, k_sz)) * 0.5).astype(np.float32)
+    A = -np.exp(rng.standard_normal(n_vh) * 0.3).astype(np.float32)
+    dt = (rng.standard_normal(n_vh) * 0.1).astype(np.float32)
+    norm_w = (1 + 0.1 * rng.standard_normal(dv)).astype(np.float32)
+    conv_state = (rng.standard_normal((B, k_sz - 1, conv_ch))).astype(np.float32)
+    ssm_state = (rng.standard_normal((B, n_vh, dv, dk)) * 0.02).astype(np.float32)
+    ref_conv = conv_state.copy()
+    ref_ssm = ssm_state.copy()
+    for step in range(5):
+        x = rng.standard_normal((B, conv_ch)).astype(np.float32)
+        z = rng.standard_normal((B, n_vh * dv)).astype(np.float32)
+        ar = rng.standard_normal((B, n_vh)).astype(np.float32)
+        br = rng.standard_normal((B, n_vh)).astype(np.float32)
+        y = vxg_b200.step_deltanet_recurrent(ctx, x, z, ar, br, w, A, dt, norm_w, conv_state,
+                                             ssm_state, n_kh, n_vh, dk, dv, k_sz, 1e-6)
+        for b in range(B):
+            ry = oracle.step_deltanet_recurrent(x[b], z[b], ar[b], br[b], w, A, dt, norm_w,
+                                                ref_conv[b], ref_ssm[b], n_kh, n_vh, dk, dv,
+                                                k_sz, 1e-6)
+            np.testing.assert_allclose(y[b], ry, atol=ATOL, rtol=RTOL, err_msg=f"step {step}")
+        assert np.array_equal(conv_state, ref_conv)   # the rolling history is a pure copy
+        np.testing.assert_allclose(ssm_state, ref_ssm, atol=ATOL, rtol=RTOL)

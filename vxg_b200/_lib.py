@@ -65,6 +65,11 @@ SIGNATURES = {
                                             _U, _U, _F, _I, _F, _P, _C, _S]),
     "vxg_attn_cuda_deltanet_step": (_I, [_P, _U, _U, _U, _U, _U, _P, _P, _P, _P, _P, _P, _P, _F,
                                          _F, _P, _P, _I, _P, _C, _S]),
+    "vxg_attn_cuda_deltanet_prefill": (_I, [_P, _U, _U, _U, _U, _U, _U, _P, _P, _P, _P, _P, _P,
+                                            _P, _F, _F, _P, _P, _I, _P, _C, _S]),
+    "vxg_attn_cuda_step_deltanet_recurrent": (_I, [_P, _U, _P, _U, _P, _P, _P, _P, _P, _P, _P, _P,
+                                                   _P, _U, _U, _U, _U, _U, _F, _P, _I, _P, _C,
+                                                   _S]),
 }
 
 _lock = threading.Lock()

@@ -373,3 +373,68 @@ def step_full_gqa_q8(ctx: Context, kv: KvQ8Pool, seq: int, q_raw, k_cur, v_cur, 
         head_dim, pos, rope_pos, rope_dim, ctypes.c_float(rope_freq_base), int(bool(rope_neox)),
         ctypes.c_float(eps), a.ptr(attn_out, np.float32, (n_head * head_dim,), "attn_out",
                                    writable=True), err.buf, err.cap), err)
+
+
+def deltanet_prefill(ctx: Context, q, k, v, beta_raw, alpha_raw, ssm_a, dt_bias, state,
+                     q_scale=None, eps=1e-6, o=None, stream=None):
+    """The DeltaNet recurrence over T tokens per sequence (the reference prefill applies the
+    step token by token, llm_prefill.rs:470-480): q,k [B][T][n_kh][dk], v [B][T][n_vh][dv],
+    beta_raw/alpha_raw [B][T][n_vh], state [B][n_vh][dv][dk] in place.  Returns o
+    [B][T][n_vh][dv]."""
+    a = _Args(state)
+    B, n_vh, dv, dk = tuple(state.shape)
+    T = (v.size if not a.device else v.numel()) // (B * n_vh * dv)
+    n_kh = (q.size if not a.device else q.numel()) // (B * T * dk)
+    if q_scale is None:
+        q_scale = 1.0 / math.sqrt(dk)
+    if o is None:
+        if a.device:
+            import torch
+            o = torch.empty((B, T, n_vh, dv), dtype=torch.float32, device=state.device)
+        else:
+            o = np.empty((B, T, n_vh, dv), np.float32)
+    err = ErrBuf()
+    rc = check(lib().vxg_attn_cuda_deltanet_prefill(
+        ctx.h, B, T, n_kh, n_vh, dk, dv, a.ptr(q, np.float32, (B, T, n_kh, dk), "q"),
+        a.ptr(k, np.float32, (B, T, n_kh, dk), "k"), a.ptr(v, np.float32, (B, T, n_vh, dv), "v"),
+        a.ptr(beta_raw, np.float32, (B, T, n_vh), "beta_raw"),
+        a.ptr(alpha_raw, np.float32, (B, T, n_vh), "alpha_raw"),
+        a.ptr(ssm_a, np.float32, (n_vh,), "ssm_a"), a.ptr(dt_bias, np.float32, (n_vh,), "dt_bias"),
+        ctypes.c_float(q_scale), ctypes.c_float(eps),
+        a.ptr(state, np.float32, (B, n_vh, dv, dk), "state", writable=True),
+        a.ptr(o, np.float32, (B, T, n_vh, dv), "o", writable=True), a.memkind, a.stream(stream),
+        err.buf, err.cap), err)
+    ctx.last_rc = rc
+    return o
+
+
+def step_deltanet_recurrent(ctx: Context, qkv_mixed, z, alpha_raw, beta_raw, ssm_conv1d, ssm_a,
+                            ssm_dt_bias, ssm_norm, conv_state, ssm_state, n_kh, n_vh, dk, dv,
+                            k_sz, eps, y_concat=None, stream=None):
+    """Drop-in for step_deltanet_recurrent (llm_ops.rs:103-121), batched: qkv_mixed [B][conv_ch],
+    z [B][n_vh*dv], alpha_raw/beta_raw [B][n_vh]; conv_state [B][k_sz-1][conv_ch] and ssm_state
+    [B][n_vh][dv][dk] are updated in place; returns y_concat [B][n_vh*dv]."""
+    a = _Args(ssm_state)
+    B = ssm_state.shape[0]
+    conv_ch = 2 * n_kh * dk + n_vh * dv
+    if y_concat is None:
+        if a.device:
+            import torch
+            y_concat = torch.empty((B, n_vh * dv), dtype=torch.float32, device=ssm_state.device)
+        else:
+            y_concat = np.empty((B, n_vh * dv), np.float32)
+    err = ErrBuf()
+    rc = check(lib().vxg_attn_cuda_step_deltanet_recurrent(
+        ctx.h, B, a.ptr(qkv_mixed, np.float32, (B, conv_ch), "qkv_mixed"), conv_ch,
+        a.ptr(z, np.float32, (B, n_vh * dv), "z"), a.ptr(alpha_raw, np.float32, (B, n_vh), "alpha_raw"),
+        a.ptr(beta_raw, np.float32, (B, n_vh), "beta_raw"),
+        a.ptr(ssm_conv1d, np.float32, (conv_ch, k_sz), "ssm_conv1d"),
+        a.ptr(ssm_a, np.float32, (n_vh,), "ssm_a"), a.ptr(ssm_dt_bias, np.float32, (n_vh,), "ssm_dt_bias"),
+        a.ptr(ssm_norm, np.float32, (dv,), "ssm_norm"),
+        a.ptr(conv_state, np.float32, (B, k_sz - 1, conv_ch), "conv_state", writable=True),
+        a.ptr(ssm_state, np.float32, (B, n_vh, dv, dk), "ssm_state", writable=True),
+        n_kh, n_vh, dk, dv, k_sz, ctypes.c_float(eps),
+        a.ptr(y_concat, np.float32, (B, n_vh * dv), "y_concat", writable=True), a.memkind,
+        a.stream(stream), err.buf, err.cap), err)
+    ctx.last_rc = rc
+    return y_concat

@@ -81,6 +81,7 @@ struct Ctx {
   DevBuf part;                  // split-KV partials
   DevBuf io;                    // device staging for host-memory calls
   DevBuf aux;                   // prepared q / gate / rope table for the drop-in step
+  DevBuf aux2;                  // DeltaNet scratch (conv output, normalised q/k, gates)
   std::set<struct Kv*> pools;   // KV pools created on this context (orphaned on destroy)
 };
 
@@ -255,14 +256,7 @@ vxg::DecodeArgs decode_args(Kv& kv, uint32_t n_batch, uint32_t n_head, const int
 vxg::Partials carve_partials(Ctx& c, const vxg::DecodeArgs& a) {
   const size_t floats = vxg::decode_partial_floats(a, c.sm_count);
   c.part.reserve(floats * sizeof(float), "cudaMalloc partials");
-  const size_t slots = floats / ((size_t)a.n_head * (2 + (size_t)a.nb * 32));
-  float* base = static_cast<float*>(c.part.p);
-  vxg::Partials p;
-  p.m = base;
-  p.l = base + slots * a.n_head;
-  p.o = base + 2 * slots * a.n_head;
-  p.n_slot = (int)slots;
-  return p;
+  return vxg::carve_partials(static_cast<float*>(c.part.p), a, c.sm_count);
 }
 
 void check_decode_shape(const Kv& kv, uint32_t n_batch, uint32_t n_head) {
@@ -327,6 +321,7 @@ void vxg_attn_cuda_destroy(void* h) {
   c->part.release();
   c->io.release();
   c->aux.release();
+  c->aux2.release();
   if (c->d_status) cudaFree(c->d_status);
   if (c->h_status) cudaFreeHost(c->h_status);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -825,13 +820,159 @@ int vxg_attn_cuda_deltanet_step(void* ctx, uint32_t n_batch, uint32_t n_kh, uint
     a.dt_bias = dt_bias;
     a.state = state;
     a.o = o;
+    a.q_bs = a.k_bs = (long long)n_kh * dk;
+    a.v_bs = a.o_bs = (long long)n_vh * dv;
+    a.g_bs = n_vh;
     a.n_batch = (int)n_batch;
+    a.n_tok = 1;
     a.n_kh = (int)n_kh;
     a.n_vh = (int)n_vh;
     a.dk = (int)dk;
     a.dv = (int)dv;
     a.eps = eps;
     a.q_scale = q_scale;
+    a.status = c.d_status;
+    check(vxg::launch_deltanet_step(a, st), "deltanet launch");
+    sg.download();
+    return finish(c, stream, st);
+  });
+}
+
+int vxg_attn_cuda_deltanet_prefill(void* ctx, uint32_t n_batch, uint32_t n_tok, uint32_t n_kh,
+                                   uint32_t n_vh, uint32_t dk, uint32_t dv, const float* q,
+                                   const float* k, const float* v, const float* beta_raw,
+                                   const float* alpha_raw, const float* ssm_a,
+                                   const float* dt_bias, float q_scale, float eps, float* state,
+                                   float* o, int memkind, void* stream, char* err, size_t cap) {
+  return guarded(ctx, stream, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    if (n_batch == 0 || n_tok == 0) return VXG_ATTN_OK;
+    require(q && k && v && beta_raw && alpha_raw && ssm_a && dt_bias && state && o,
+            VXG_ATTN_ERR_NULL_PTR, "null input");
+    require(n_kh > 0 && n_vh > 0 && n_vh % n_kh == 0, VXG_ATTN_ERR_INVALID_OPTION,
+            "n_vh must be a positive multiple of n_kh");
+    require(dk == 64 || dk == 128 || dk == 256, VXG_ATTN_ERR_UNSUPPORTED,
+            "dk must be 64, 128 or 256");
+    require(dv > 0 && dv % 32 == 0, VXG_ATTN_ERR_UNSUPPORTED, "dv must be a multiple of 32");
+    cudaStream_t st = pick_stream(c, stream);
+    const bool host = memkind == VXG_ATTN_MEM_HOST;
+    if (!host)
+      require(((uintptr_t)state % 16) == 0, VXG_ATTN_ERR_INVALID_OPTION,
+              "state must be 16-byte aligned");
+    const size_t bt = (size_t)n_batch * n_tok;
+    Stager sg(c, st, host);
+    sg.in(q, bt * n_kh * dk * sizeof(float));
+    sg.in(k, bt * n_kh * dk * sizeof(float));
+    sg.in(v, bt * n_vh * dv * sizeof(float));
+    sg.in(beta_raw, bt * n_vh * sizeof(float));
+    sg.in(alpha_raw, bt * n_vh * sizeof(float));
+    sg.in(ssm_a, n_vh * sizeof(float));
+    sg.in(dt_bias, n_vh * sizeof(float));
+    sg.inout(state, (size_t)n_batch * n_vh * dv * dk * sizeof(float));
+    sg.out(o, bt * n_vh * dv * sizeof(float));
+    sg.upload();
+    vxg::DeltaNetArgs a{};
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.beta_raw = beta_raw;
+    a.alpha_raw = alpha_raw;
+    a.ssm_a = ssm_a;
+    a.dt_bias = dt_bias;
+    a.state = state;
+    a.o = o;
+    a.q_ts = a.k_ts = (long long)n_kh * dk;
+    a.q_bs = a.k_bs = (long long)n_tok * n_kh * dk;
+    a.v_ts = a.o_ts = (long long)n_vh * dv;
+    a.v_bs = a.o_bs = (long long)n_tok * n_vh * dv;
+    a.g_ts = n_vh;
+    a.g_bs = (long long)n_tok * n_vh;
+    a.n_batch = (int)n_batch;
+    a.n_tok = (int)n_tok;
+    a.n_kh = (int)n_kh;
+    a.n_vh = (int)n_vh;
+    a.dk = (int)dk;
+    a.dv = (int)dv;
+    a.eps = eps;
+    a.q_scale = q_scale;
+    a.status = c.d_status;
+    c.aux2.reserve(vxg::deltanet_prefill_scratch_bytes(a), "cudaMalloc deltanet scratch");
+    check(vxg::launch_deltanet_prefill(a, c.aux2.p, st), "deltanet prefill launch");
+    sg.download();
+    return finish(c, stream, st);
+  });
+}
+
+int vxg_attn_cuda_step_deltanet_recurrent(
+    void* ctx, uint32_t n_batch, const float* qkv_mixed, uint32_t conv_ch, const float* z,
+    const float* alpha_raw, const float* beta_raw, const float* ssm_conv1d, const float* ssm_a,
+    const float* ssm_dt_bias, const float* ssm_norm, float* conv_state, float* ssm_state,
+    uint32_t n_kh, uint32_t n_vh, uint32_t dk, uint32_t dv, uint32_t k_sz, float eps,
+    float* y_concat, int memkind, void* stream, char* err, size_t cap) {
+  return guarded(ctx, stream, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    if (n_batch == 0) return VXG_ATTN_OK;
+    require(qkv_mixed && z && alpha_raw && beta_raw && ssm_conv1d && ssm_a && ssm_dt_bias &&
+                ssm_norm && conv_state && ssm_state && y_concat,
+            VXG_ATTN_ERR_NULL_PTR, "null input");
+    require(n_kh > 0 && n_vh > 0 && n_vh % n_kh == 0, VXG_ATTN_ERR_INVALID_OPTION,
+            "n_vh must be a positive multiple of n_kh");
+    require(dk == 64 || dk == 128 || dk == 256, VXG_ATTN_ERR_UNSUPPORTED,
+            "dk must be 64, 128 or 256");
+    require(dv > 0 && dv % 32 == 0 && dv <= 256, VXG_ATTN_ERR_UNSUPPORTED,
+            "dv must be a multiple of 32, at most 256");
+    require(k_sz >= 2, VXG_ATTN_ERR_INVALID_OPTION, "k_sz must be at least 2");
+    require(conv_ch == 2 * n_kh * dk + n_vh * dv, VXG_ATTN_ERR_INVALID_OPTION,
+            "conv_ch must equal 2 * n_kh * dk + n_vh * dv (llm_ops.rs:139-143)");
+    cudaStream_t st = pick_stream(c, stream);
+    const bool host = memkind == VXG_ATTN_MEM_HOST;
+    if (!host)
+      require(((uintptr_t)ssm_state % 16) == 0, VXG_ATTN_ERR_INVALID_OPTION,
+              "ssm_state must be 16-byte aligned");
+    const size_t ydim = (size_t)n_vh * dv;
+    Stager sg(c, st, host);
+    sg.in(qkv_mixed, (size_t)n_batch * conv_ch * sizeof(float));
+    sg.in(z, n_batch * ydim * sizeof(float));
+    sg.in(alpha_raw, (size_t)n_batch * n_vh * sizeof(float));
+    sg.in(beta_raw, (size_t)n_batch * n_vh * sizeof(float));
+    sg.in(ssm_conv1d, (size_t)conv_ch * k_sz * sizeof(float));
+    sg.in(ssm_a, n_vh * sizeof(float));
+    sg.in(ssm_dt_bias, n_vh * sizeof(float));
+    sg.in(ssm_norm, dv * sizeof(float));
+    sg.inout(conv_state, (size_t)n_batch * (k_sz - 1) * conv_ch * sizeof(float));
+    sg.inout(ssm_state, (size_t)n_batch * n_vh * dv * dk * sizeof(float));
+    sg.out(y_concat, n_batch * ydim * sizeof(float));
+    sg.upload();
+    c.aux2.reserve((size_t)n_batch * conv_ch * sizeof(float) + 256, "cudaMalloc conv scratch");
+    float* conv_out = static_cast<float*>(c.aux2.p);
+    check(vxg::launch_deltanet_conv(qkv_mixed, ssm_conv1d, conv_state, conv_out, (int)n_batch,
+                                    (int)conv_ch, (int)k_sz, st),
+          "conv launch");
+    const size_t qk_dim = (size_t)n_kh * dk;
+    vxg::DeltaNetArgs a{};
+    a.q = conv_out;
+    a.k = conv_out + qk_dim;
+    a.v = conv_out + 2 * qk_dim;
+    a.beta_raw = beta_raw;
+    a.alpha_raw = alpha_raw;
+    a.ssm_a = ssm_a;
+    a.dt_bias = ssm_dt_bias;
+    a.state = ssm_state;
+    a.o = nullptr;
+    a.z = z;
+    a.ssm_norm = ssm_norm;
+    a.y = y_concat;
+    a.q_bs = a.k_bs = a.v_bs = conv_ch;
+    a.o_bs = (long long)ydim;
+    a.g_bs = n_vh;
+    a.n_batch = (int)n_batch;
+    a.n_tok = 1;
+    a.n_kh = (int)n_kh;
+    a.n_vh = (int)n_vh;
+    a.dk = (int)dk;
+    a.dv = (int)dv;
+    a.eps = eps;
+    a.q_scale = 1.0f / sqrtf((float)dk);
     a.status = c.d_status;
     check(vxg::launch_deltanet_step(a, st), "deltanet launch");
     sg.download();

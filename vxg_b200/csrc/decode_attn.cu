@@ -307,6 +307,13 @@ __global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs
       }
     }
     if (lane == 31) sm.prefix[B] = incl;
+    __syncwarp();
+    if (blockIdx.x == 0) {  // published for the combine pass: unit prefix and CTA unit ranges
+      for (int i = lane; i <= B; i += 32) part.prefix[i] = sm.prefix[i];
+      const long long Utot = sm.prefix[B];
+      for (int i = lane; i <= (int)gridDim.x; i += 32)
+        part.prefix[B + 1 + i] = (int)((long long)i * Utot / gridDim.x);
+    }
   }
   if (tid == 0) {
     for (int i = 0; i < NBAR; ++i) mbar_init(&sm.full[i], 1);
@@ -635,143 +642,207 @@ __global__ void __launch_bounds__(256) decode_combine(DecodeArgs a, Partials par
   }
 }
 
-// Fast-path combine: grid (batch entry, 64-dim chunk); thread = (dim, 4-head quad).  CTA i of
-// the split pass owned units [i*U/n_cta, (i+1)*U/n_cta); for each such CTA meeting entry b,
-// slots (i + b)*SUBS + sub hold the partials of its 4 sub-tiles, o stored [dim][head].
+// Fast-path combine.  CTA i of the split pass owned units [i*U/n_cta, (i+1)*U/n_cta) of the unit
+// prefix the split pass published in part.prefix; for each such CTA meeting entry b, slots
+// (i + b)*SUBS + sub hold the partials of its sub-tiles, o stored [dim][head].
+// Grid (entry, 64-dim chunk, slot split z); thread = (dim, slot lane); CTA z merges the slots
+// k = z, z + S, ... of its entry.  With S == 1 it writes the result; otherwise an intermediate
+// (m, l, o) that decode_fast_combine_final merges.
+namespace {
+constexpr int kCombineSplitMax = 32;
+constexpr int kCombineDims = 64;
+constexpr int kCombineLanes = 4;   // slot lanes per output dim
+constexpr int kCombineStage = 128; // slots whose m / l / factors are staged at a time
+}
 __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partials part, int n_cta,
-                                                           const float* gate, float* out,
+                                                           int S, const float* gate, float* out,
                                                            float* m_out, float* l_out,
                                                            float* o_out) {
   using namespace fast;
   constexpr int H = NKV * G;
-  constexpr int MAXS = 256 * SUBS;  // partial slots merged per entry (CTAs meeting one entry)
-  constexpr int CH = 128;           // slots whose merge factors are staged at a time
-  const int b = blockIdx.x, tid = threadIdx.x;
-  const int d = blockIdx.y * 64 + (tid >> 2), hq = tid & 3;
-  __shared__ long long red[2][256];
+  constexpr int MAXS = 256 * SUBS;
+  const int b = blockIdx.x, z = blockIdx.z;
+  const int tid = threadIdx.x, dl = tid % kCombineDims, sl = tid / kCombineDims;
+  const int d = blockIdx.y * kCombineDims + dl;
   __shared__ int s_slot[MAXS];
-  __shared__ float s_f[CH][H];
-  __shared__ float s_l[CH][H];
-  __shared__ float s_Mnew[H];
   __shared__ int s_n;
-  __shared__ float s_M[H], s_L[H];
-  const int len = entry_len(a, b);
-  if (tid == 0 && blockIdx.y == 0 && !entry_valid(a, b)) atomicOr(a.status, kStatusBadIndex);
-  long long before = 0, tot = 0;
-  for (int i = tid; i < a.n_batch; i += 256) {
-    const long long un = (entry_len(a, i) + ST - 1) / ST;
-    tot += un;
-    if (i < b) before += un;
-  }
-  red[0][tid] = before;
-  red[1][tid] = tot;
+  __shared__ float s_f[kCombineStage][H];
+  __shared__ float s_l[kCombineStage][H];
+  __shared__ float s_M[H];
+  __shared__ float s_acc[kCombineLanes][kCombineDims][H + 1];
+  __shared__ int s_ilo;
+  __shared__ int cta_start[512 + 1];  // unit ranges of the split pass's CTAs (n_cta <= 512)
+  for (int i = tid; i <= n_cta; i += 256) cta_start[i] = part.prefix[a.n_batch + 1 + i];
   __syncthreads();
-  for (int st = 128; st > 0; st >>= 1) {
-    if (tid < st) {
-      red[0][tid] += red[0][tid + st];
-      red[1][tid] += red[1][tid + st];
-    }
-    __syncthreads();
-  }
   if (tid == 0) {
-    const long long U = red[1][0], P0 = red[0][0];
-    const long long P1 = P0 + (len + ST - 1) / ST;
-    int n = 0;
+    if (blockIdx.y == 0 && z == 0 && !entry_valid(a, b)) atomicOr(a.status, kStatusBadIndex);
+    const int P0 = part.prefix[b], P1 = part.prefix[b + 1];
+    int n = 0, ilo = 0;
     if (P1 > P0) {
-      long long ilo = ((P0 + 1) * n_cta + U - 1) / U - 1;
-      long long ihi = (P1 * n_cta + U - 1) / U - 1;
-      if (ilo < 0) ilo = 0;
-      if (ihi > n_cta - 1) ihi = n_cta - 1;
-      for (long long i = ilo; i <= ihi && n + SUBS <= MAXS; ++i) {
-        const long long r0 = i * U / n_cta, r1 = (i + 1) * U / n_cta;
-        if (max(r0, P0) < min(r1, P1))
-          for (int s2 = 0; s2 < SUBS; ++s2) s_slot[n++] = (int)((i + b) * SUBS + s2);
+      // first CTA whose range ends after P0, last CTA whose range starts before P1
+      int lo = 0, hi = n_cta - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (cta_start[mid + 1] > P0) hi = mid;
+        else lo = mid + 1;
       }
+      ilo = lo;
+      lo = ilo;
+      hi = n_cta - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (cta_start[mid] < P1) lo = mid;
+        else hi = mid - 1;
+      }
+      n = min((lo - ilo + 1) * SUBS, MAXS);
     }
+    s_ilo = ilo;
     s_n = n;
   }
   __syncthreads();
+  for (int k = tid; k < s_n; k += 256) {
+    const int i = s_ilo + k / SUBS;
+    // a CTA with an empty range (possible only when units < CTAs) wrote no partials
+    s_slot[k] = cta_start[i] < cta_start[i + 1] ? (i + b) * SUBS + k % SUBS : -1;
+  }
+  __syncthreads();
   const int ns = s_n;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float Lp = 0.f;
-  // Slots are processed CH at a time: their m and l are staged in shared memory by all threads
-  // (independent loads), the running max per head is kept, and the accumulators are rescaled
-  // when it grows -- an online log-sum-exp over the slots.
-  float Mrun = -INFINITY;  // per head (threads < H), and per quad head via s_M
+  const int nz = ns > z ? (ns - z + S - 1) / S : 0;  // this split's slots: k = z + S*j
+  // running max per head over this split's slots: m staged through shared memory by all
+  // threads (independent loads), then reduced per head
   if (tid < H) s_M[tid] = -INFINITY;
-  for (int k0 = 0; k0 < ns; k0 += CH) {
-    const int nk = min(CH, ns - k0);
+  for (int j0 = 0; j0 < nz; j0 += kCombineStage) {
+    const int nk = min(kCombineStage, nz - j0);
     for (int idx = tid; idx < nk * H; idx += 256) {
-      const int k = idx / H, h = idx % H;
-      s_f[k][h] = part.m[(size_t)s_slot[k0 + k] * H + h];
-      s_l[k][h] = part.l[(size_t)s_slot[k0 + k] * H + h];
+      const int slot = s_slot[z + S * (j0 + idx / H)];
+      s_f[idx / H][idx % H] = slot < 0 ? -INFINITY : part.m[(size_t)slot * H + idx % H];
     }
     __syncthreads();
     if (tid < H) {
-      float M = Mrun;
+      float M = s_M[tid];
       for (int k = 0; k < nk; ++k) M = fmaxf(M, s_f[k][tid]);
-      s_Mnew[tid] = M;
-    }
-    __syncthreads();
-    // rescale what was accumulated so far, then turn the staged m into merge factors
-    float sc[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float mo = s_M[4 * hq + e], mn = s_Mnew[4 * hq + e];
-      sc[e] = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
-    }
-    acc.x *= sc[0];
-    acc.y *= sc[1];
-    acc.z *= sc[2];
-    acc.w *= sc[3];
-    if (tid < H) {
-      const float mo = s_M[tid], mn = s_Mnew[tid];
-      Lp *= (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
-      Mrun = mn;
-    }
-    __syncthreads();
-    for (int idx = tid; idx < nk * H; idx += 256) {
-      const int k = idx / H, h = idx % H;
-      const float mk = s_f[k][h], mn = s_Mnew[h];
-      s_f[k][h] = (mk == -INFINITY || mn == -INFINITY) ? 0.f : exp2f(mk - mn);
-    }
-    __syncthreads();
-    if (tid < H) {
-      s_M[tid] = Mrun;
-      for (int k = 0; k < nk; ++k) Lp = fmaf(s_l[k][tid], s_f[k][tid], Lp);
-    }
-#pragma unroll 4
-    for (int k = 0; k < nk; ++k) {
-      const float4 x = *reinterpret_cast<const float4*>(
-          part.o + ((size_t)s_slot[k0 + k] * HD + d) * H + 4 * hq);
-      const float* f = &s_f[k][4 * hq];
-      acc.x = fmaf(x.x, f[0], acc.x);
-      acc.y = fmaf(x.y, f[1], acc.y);
-      acc.z = fmaf(x.z, f[2], acc.z);
-      acc.w = fmaf(x.w, f[3], acc.w);
+      s_M[tid] = M;
     }
     __syncthreads();
   }
-  if (tid < H) s_L[tid] = Lp;
-  __syncthreads();
-  const float* ap = &acc.x;
+  float acc[H];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int h = 4 * hq + e;
-    const size_t oi = ((size_t)b * H + h) * HD + d;
+  for (int h = 0; h < H; ++h) acc[h] = 0.f;
+  float Lp = 0.f;
+  for (int j0 = 0; j0 < nz; j0 += kCombineStage) {
+    const int nk = min(kCombineStage, nz - j0);
+    for (int idx = tid; idx < nk * H; idx += 256) {
+      const int k = idx / H, h = idx % H;
+      const int slot = s_slot[z + S * (j0 + k)];
+      if (slot < 0) {
+        s_f[k][h] = 0.f;
+        s_l[k][h] = 0.f;
+        continue;
+      }
+      const size_t sl2 = (size_t)slot * H + h;
+      const float mk = part.m[sl2], M = s_M[h];
+      s_f[k][h] = (mk == -INFINITY || M == -INFINITY) ? 0.f : exp2f(mk - M);
+      s_l[k][h] = part.l[sl2];
+    }
+    __syncthreads();
+    if (tid < H)
+      for (int k = 0; k < nk; ++k) Lp = fmaf(s_l[k][tid], s_f[k][tid], Lp);
+#pragma unroll 2
+    for (int k = sl; k < nk; k += kCombineLanes) {
+      const int slot = s_slot[z + S * (j0 + k)];
+      if (slot < 0) continue;
+      const float4* orow = reinterpret_cast<const float4*>(part.o + ((size_t)slot * HD + d) * H);
+#pragma unroll
+      for (int v = 0; v < H / 4; ++v) {
+        const float4 x = orow[v];
+        acc[4 * v] = fmaf(x.x, s_f[k][4 * v], acc[4 * v]);
+        acc[4 * v + 1] = fmaf(x.y, s_f[k][4 * v + 1], acc[4 * v + 1]);
+        acc[4 * v + 2] = fmaf(x.z, s_f[k][4 * v + 2], acc[4 * v + 2]);
+        acc[4 * v + 3] = fmaf(x.w, s_f[k][4 * v + 3], acc[4 * v + 3]);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int h = 0; h < H; ++h) s_acc[sl][dl][h] = acc[h];
+  if (tid < H) s_f[0][tid] = Lp;
+  __syncthreads();
+  // thread t -> 4 outputs (head h, dims dd..dd+3 of the chunk): sum over the slot lanes
+  for (int oidx = tid; oidx < H * kCombineDims; oidx += 256) {
+    const int h = oidx / kCombineDims, dd = oidx % kCombineDims;
+    float O = 0.f;
+#pragma unroll
+    for (int s2 = 0; s2 < kCombineLanes; ++s2) O += s_acc[s2][dd][h];
+    const float L = s_f[0][h], M = s_M[h];
+    const int dim = blockIdx.y * kCombineDims + dd;
+    if (S > 1) {
+      const size_t iz = ((size_t)b * S + z) * H + h;
+      float* im = part.inter;
+      float* il = im + (size_t)a.n_batch * S * H;
+      float* io = il + (size_t)a.n_batch * S * H;
+      io[iz * HD + dim] = O;
+      if (dim == 0) {
+        im[iz] = M;
+        il[iz] = L;
+      }
+      continue;
+    }
+    const size_t oi = ((size_t)b * H + h) * HD + dim;
     if (m_out) {
-      o_out[oi] = ap[e];
-      if (d == 0) {
-        m_out[(size_t)b * H + h] = s_M[h];
-        l_out[(size_t)b * H + h] = s_L[h];
+      o_out[oi] = O;
+      if (dim == 0) {
+        m_out[(size_t)b * H + h] = M;
+        l_out[(size_t)b * H + h] = L;
       }
     } else {
-      const float L = s_L[h];
-      float r = (L > 0.f || L != L) ? ap[e] / L : 0.f;  // NaN partials stay NaN
+      float r = (L > 0.f || L != L) ? O / L : 0.f;  // NaN partials stay NaN
       if (gate) r *= 1.0f / (1.0f + expf(-gate[oi]));
       if (!isfinite(r)) atomicOr(a.status, kStatusNonFinite);
       out[oi] = r;
     }
+  }
+}
+
+// Merge of the S intermediates per entry: grid (entry, head), thread = dim.
+__global__ void __launch_bounds__(256) decode_fast_combine_final(DecodeArgs a, Partials part,
+                                                                 int S, const float* gate,
+                                                                 float* out, float* m_out,
+                                                                 float* l_out, float* o_out) {
+  using namespace fast;
+  constexpr int H = NKV * G;
+  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const float* im = part.inter;
+  const float* il = im + (size_t)a.n_batch * S * H;
+  const float* io = il + (size_t)a.n_batch * S * H;
+  __shared__ float s_m[kCombineSplitMax], s_l[kCombineSplitMax];
+  if (d < S) {
+    s_m[d] = im[((size_t)b * S + d) * H + h];
+    s_l[d] = il[((size_t)b * S + d) * H + h];
+  }
+  __syncthreads();
+  float M = -INFINITY;
+  for (int z = 0; z < S; ++z) M = fmaxf(M, s_m[z]);
+  float L = 0.f, O = 0.f;
+  if (M != -INFINITY)
+#pragma unroll 4
+    for (int z = 0; z < S; ++z) {
+      const float mz = s_m[z];
+      const float f = mz == -INFINITY ? 0.f : exp2f(mz - M);
+      L = fmaf(s_l[z], f, L);
+      O = fmaf(io[(((size_t)b * S + z) * H + h) * HD + d], f, O);
+    }
+  const size_t oi = ((size_t)b * H + h) * HD + d;
+  if (m_out) {
+    o_out[oi] = O;
+    if (d == 0) {
+      m_out[(size_t)b * H + h] = M;
+      l_out[(size_t)b * H + h] = L;
+    }
+  } else {
+    float r = (L > 0.f || L != L) ? O / L : 0.f;
+    if (gate) r *= 1.0f / (1.0f + expf(-gate[oi]));
+    if (!isfinite(r)) atomicOr(a.status, kStatusNonFinite);
+    out[oi] = r;
   }
 }
 
@@ -806,7 +877,7 @@ __global__ void __launch_bounds__(256) lse_combine_kernel(int n_parts, int n_row
 namespace {
 bool fast_applies(const DecodeArgs& a) {
   return a.nb == fast::NB && a.n_kv == fast::NKV && a.n_head == fast::NKV * fast::G &&
-         a.n_batch <= fast::MAXB;
+         a.n_batch <= fast::MAXB;  // (and at most 512 SMs: the combine stages their ranges)
 }
 int heads_per_cta(int G) {
   int hpc = 8;
@@ -830,12 +901,60 @@ int generic_max_split(const DecodeArgs& a) {
 }
 }  // namespace
 
+namespace {
+// CTAs of the persistent split pass (the combine stages their unit ranges: at most 512).
+int fast_grid(int sm_count) { return std::max(1, std::min(sm_count, 512)); }
+// Slot splits of the fast combine: aim for >= 128 CTAs of 64 output dims each.
+int combine_splits(const DecodeArgs& a) {
+  const int per = std::max(1, a.n_batch * (fast::HD / kCombineDims));
+  return std::max(1, std::min(kCombineSplitMax, (128 + per - 1) / per));
+}
+}  // namespace
+
 size_t decode_partial_floats(const DecodeArgs& a, int sm_count) {
   size_t slots;
   if (fast_applies(a)) slots = ((size_t)sm_count + a.n_batch) * fast::SUBS;
   else slots = (size_t)a.n_batch * generic_max_split(a);
-  return slots * a.n_head * (2 + (size_t)a.nb * 32);
+  size_t f = slots * a.n_head * (2 + (size_t)a.nb * 32);
+  const int S = fast_applies(a) ? combine_splits(a) : 1;
+  if (S > 1) f += (size_t)a.n_batch * S * a.n_head * (2 + fast::HD);
+  if (fast_applies(a)) f += (size_t)a.n_batch + sm_count + 64;  // published prefix + CTA ranges
+  return f;
 }
+
+Partials carve_partials(float* base, const DecodeArgs& a, int sm_count) {
+  size_t slots;
+  if (fast_applies(a)) slots = ((size_t)sm_count + a.n_batch) * fast::SUBS;
+  else slots = (size_t)a.n_batch * generic_max_split(a);
+  Partials p;
+  p.m = base;
+  p.l = base + slots * a.n_head;
+  p.o = base + 2 * slots * a.n_head;
+  p.inter = p.o + slots * a.n_head * (size_t)a.nb * 32;
+  p.n_slot = (int)slots;
+  p.prefix = nullptr;
+  if (fast_applies(a)) {
+    const int S = combine_splits(a);
+    float* after = p.inter + (S > 1 ? (size_t)a.n_batch * S * a.n_head * (2 + fast::HD) : 0);
+    p.prefix = reinterpret_cast<int*>(after);
+  }
+  return p;
+}
+
+namespace {
+cudaError_t launch_fast_combine(const DecodeArgs& a, const Partials& part, int sm_count,
+                                const float* gate, float* out, float* m_out, float* l_out,
+                                float* o_out, cudaStream_t st) {
+  const int S = combine_splits(a);
+  decode_fast_combine<<<dim3(a.n_batch, fast::HD / kCombineDims, S), 256, 0, st>>>(
+      a, part, fast_grid(sm_count), S, gate, out, m_out, l_out, o_out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || S == 1) return e;
+  decode_fast_combine_final<<<dim3(a.n_batch, fast::NKV * fast::G), fast::HD, 0, st>>>(
+      a, part, S, gate, out, m_out, l_out, o_out);
+  return cudaGetLastError();
+}
+}  // namespace
 
 static cudaError_t run_split(const DecodeArgs& a, const Partials& p, int sm_count,
                              int force_generic, cudaStream_t st, int* mode, int* max_split) {
@@ -852,7 +971,7 @@ static cudaError_t run_split(const DecodeArgs& a, const Partials& p, int sm_coun
     }
     *mode = 1;
     *max_split = 0;
-    decode_fast_split<<<sm_count, fast::THREADS, sizeof(fast::Smem), st>>>(a, p);
+    decode_fast_split<<<fast_grid(sm_count), fast::THREADS, sizeof(fast::Smem), st>>>(a, p);
     return cudaGetLastError();
   }
   *mode = 0;
@@ -881,8 +1000,7 @@ cudaError_t launch_decode(const DecodeArgs& a, const Partials& part, const float
   if (e != cudaSuccess) return e;
   if (ev1) cudaEventRecord(ev1, st);
   if (mode == 1)
-    decode_fast_combine<<<dim3(a.n_batch, fast::HD / 64), 256, 0, st>>>(
-        a, part, sm_count, gate, out, nullptr, nullptr, nullptr);
+    return launch_fast_combine(a, part, sm_count, gate, out, nullptr, nullptr, nullptr, st);
   else
     decode_combine<<<dim3(a.n_batch, a.n_head), 256, 0, st>>>(a, part, max_split, gate, out,
                                                               nullptr, nullptr, nullptr);
@@ -897,8 +1015,7 @@ cudaError_t launch_decode_partial(const DecodeArgs& a, const Partials& part, flo
   cudaError_t e = run_split(a, part, sm_count, force_generic, st, &mode, &max_split);
   if (e != cudaSuccess) return e;
   if (mode == 1)
-    decode_fast_combine<<<dim3(a.n_batch, fast::HD / 64), 256, 0, st>>>(
-        a, part, sm_count, nullptr, nullptr, m_out, l_out, o_out);
+    return launch_fast_combine(a, part, sm_count, nullptr, nullptr, m_out, l_out, o_out, st);
   else
     decode_combine<<<dim3(a.n_batch, a.n_head), 256, 0, st>>>(a, part, max_split, nullptr,
                                                               nullptr, m_out, l_out, o_out);

@@ -32,11 +32,14 @@ struct Partials {
   float* m;   // [n_slot][n_head]
   float* l;   // [n_slot][n_head]
   float* o;   // [n_slot][n_head][hd]
+  float* inter; // second-level merge scratch of the fast combine
+  int* prefix;  // unit prefix over the batch, published by the fast split pass
   int n_slot; // slots available
 };
 
-// Bytes of partial storage the split-KV pass needs for these args.
+// Floats of partial storage the split-KV pass needs for these args, and its carving.
 size_t decode_partial_floats(const DecodeArgs& a, int sm_count);
+Partials carve_partials(float* base, const DecodeArgs& a, int sm_count);
 
 // Split-KV pass then LSE combine into out[n_batch][n_head][hd] (gate optional, same shape).
 // `force_generic` selects the portable kernel even when the fast path applies.
@@ -58,20 +61,34 @@ cudaError_t launch_lse_combine(int n_parts, int n_rows, int hd, const float* m, 
 
 // deltanet.cu ------------------------------------------------------------------------------
 struct DeltaNetArgs {
-  const float* q;          // [n_batch][n_kh][dk] (before L2 norm)
-  const float* k;          // [n_batch][n_kh][dk]
-  const float* v;          // [n_batch][n_vh][dv]
-  const float* beta_raw;   // [n_batch][n_vh]
-  const float* alpha_raw;  // [n_batch][n_vh]
+  // Element (b, t, head, i) of q / k is at q + b*q_bs + t*q_ts + head*dk + i (k likewise);
+  // v, o, z, y use (v_bs, v_ts) / (o_bs, o_ts) with head*dv; beta_raw, alpha_raw use (g_bs, g_ts).
+  const float* q;          // before L2 norm
+  const float* k;
+  const float* v;
+  const float* beta_raw;
+  const float* alpha_raw;
   const float* ssm_a;      // [n_vh]
   const float* dt_bias;    // [n_vh]
   float* state;            // [n_batch][n_vh][dv][dk] updated in place
-  float* o;                // [n_batch][n_vh][dv]
-  int n_batch, n_kh, n_vh, dk, dv;
+  float* o;                // S_new q (not written by the decode step when y != nullptr)
+  const float* z;          // epilogue gate input (optional, with y)
+  const float* ssm_norm;   // [dv] RMSNorm weight (with y)
+  float* y;                // optional: RMSNorm(o) * ssm_norm * SiLU(z)
+  long long q_bs, q_ts, k_bs, k_ts, v_bs, v_ts, g_bs, g_ts, o_bs, o_ts;
+  int n_batch, n_tok, n_kh, n_vh, dk, dv;
   float eps, q_scale;
   uint32_t* status;
 };
+// One token per sequence (t = 0), state streamed from / to HBM.
 cudaError_t launch_deltanet_step(const DeltaNetArgs& a, cudaStream_t stream);
+// n_tok tokens per sequence with the state held on chip; needs deltanet_prefill_scratch_bytes of
+// device scratch.  Writes o (and y with the epilogue when y != nullptr).
+size_t deltanet_prefill_scratch_bytes(const DeltaNetArgs& a);
+cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, cudaStream_t stream);
+// conv1d + SiLU over the rolling history (llm_ops.rs:122-137), batched.
+cudaError_t launch_deltanet_conv(const float* x, const float* w, float* conv_state, float* out,
+                                 int n_batch, int conv_ch, int k_sz, cudaStream_t stream);
 
 // prep.cu ----------------------------------------------------------------------------------
 // q/k prologue of step_full_gqa_q8 for one token: rope_cs = host-computed (cos, sin) pairs.

@@ -131,13 +131,8 @@ extern "C" int vxg_attn_cuda_q8_decode_noalloc(
   }
   uint32_t* status = reinterpret_cast<uint32_t*>(ds.base);
   a.status = status;
-  const size_t slots = floats / ((size_t)a.n_head * (2 + (size_t)a.nb * 32));
-  float* pbase = reinterpret_cast<float*>(ds.base + kStatusBytes);
-  vxg::Partials part;
-  part.m = pbase;
-  part.l = pbase + slots * a.n_head;
-  part.o = pbase + 2 * slots * a.n_head;
-  part.n_slot = (int)slots;
+  vxg::Partials part =
+      vxg::carve_partials(reinterpret_cast<float*>(ds.base + kStatusBytes), a, ds.sm_count);
 
   // NULL stream: run on the legacy default stream and wait, so the status can be reported.
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy;

@@ -1,0 +1,103 @@
+"""Multi-GPU layouts of the decode path (one process per GPU, torch.distributed plumbing).
+
+* Sequence sharding (batched decode, DeltaNet): each rank owns whole sequences; no collective
+  on the data path.  ``shard_sequences`` gives a rank's contiguous share.
+* KV-range split of one long context: rank r owns tokens [r*span, (r+1)*span) of the sequence
+  in its own KV pool.  A decode step appends the new token on the rank that owns its
+  position, every rank computes the split-KV partial (m, l, o) of the query over its range,
+  the partials are all-gathered (NCCL over NVLink on GPUs; any backend works for the host
+  logic), and every rank merges them with the log-sum-exp combine.  The exchanged data is
+  n_head * (head_dim + 2) floats per rank, so the collective is latency-bound.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+
+def shard_sequences(n_seq: int, world: int, rank: int) -> range:
+    """Contiguous, balanced share of sequence ids for ``rank``."""
+    base, extra = divmod(n_seq, world)
+    start = rank * base + min(rank, extra)
+    return range(start, start + base + (1 if rank < extra else 0))
+
+
+class KvRange:
+    """Token-range ownership of one sequence split over ``world`` ranks."""
+
+    def __init__(self, capacity: int, world: int, rank: int):
+        self.world, self.rank = world, rank
+        self.span = int(math.ceil(capacity / world))
+        self.begin = rank * self.span
+
+    def owner(self, pos: int) -> int:
+        return min(pos // self.span, self.world - 1)
+
+    def local_pos(self, pos: int) -> int:
+        return pos - self.owner(pos) * self.span
+
+    def local_len(self, ctx_len: int) -> int:
+        """Tokens of [0, ctx_len) that live on this rank."""
+        return int(max(0, min(self.span, ctx_len - self.begin)))
+
+
+def pack_partials(m, l, o):
+    """(m [R], l [R], o [R][hd]) -> one flat tensor [R*(hd+2)] for a single collective."""
+    import torch
+    return torch.cat([m.reshape(-1), l.reshape(-1), o.reshape(-1)])
+
+
+def unpack_partials(buf, world: int, rows: int, hd: int):
+    """[world * rows*(hd+2)] -> m, l [world][rows], o [world][rows][hd]."""
+    per = rows * (hd + 2)
+    b = buf.reshape(world, per)
+    return (b[:, :rows].contiguous(), b[:, rows:2 * rows].contiguous(),
+            b[:, 2 * rows:].reshape(world, rows, hd).contiguous())
+
+
+def all_gather_partials(m, l, o, group=None):
+    """All-gather this rank's partials; returns m, l [world][R], o [world][R][hd]."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rows, hd = o.reshape(-1, o.shape[-1]).shape
+    send = pack_partials(m, l, o)
+    recv = torch.empty(world * send.numel(), dtype=send.dtype, device=send.device)
+    dist.all_gather_into_tensor(recv, send, group=group)
+    return unpack_partials(recv, world, rows, hd)
+
+
+class LongContextDecoder:
+    """One long sequence split by KV range across the ranks of the default process group.
+
+    Owns this rank's slice as a one-sequence KvQ8Pool; ``step`` appends the new token where it
+    belongs and returns the merged attention output (every rank gets it)."""
+
+    def __init__(self, ctx, capacity: int, n_head: int, n_head_kv: int, head_dim: int,
+                 world: int, rank: int, group=None):
+        from .attn import KvQ8Pool
+        self.ctx = ctx
+        self.range = KvRange(capacity, world, rank)
+        self.pool = KvQ8Pool(ctx, 1, n_head_kv, head_dim, self.range.span)
+        self.n_head, self.head_dim = n_head, head_dim
+        self.group = group
+        import torch
+        self._seq = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self._begin = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self._end = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self._pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def step(self, pos: int, q, k_new, v_new, scale=None):
+        """Append (k_new, v_new) at ``pos`` (on its owner) and attend q over [0, pos]."""
+        from .attn import lse_combine
+        r = self.range
+        if r.owner(pos) == r.rank:
+            self._pos.fill_(r.local_pos(pos))
+            self.pool.append(self._seq, self._pos, k_new.reshape(1, 1, -1, self.head_dim),
+                             v_new.reshape(1, 1, -1, self.head_dim))
+        self._end.fill_(r.local_len(pos + 1))
+        m, l, o = self.pool.decode_partial(self._seq, self._begin, self._end,
+                                           q.reshape(1, self.n_head, self.head_dim), scale=scale)
+        M, L, O = all_gather_partials(m, l, o, self.group)
+        return lse_combine(self.ctx, M, L, O)
