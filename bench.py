@@ -9,7 +9,7 @@ per GPU, each with its own 64 sequences (weak scaling, no data-path collective);
 ranks of the device-timed region.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|long|deltanet]
+                    [--workload decode|long|deltanet|prefill]
 """
 from __future__ import annotations
 
@@ -407,6 +407,74 @@ def run_long(args, world, rank, local):
             "gpu_launches": (3 if world == 1 else 4) * K, "clocks": sampler.summary()}
 
 
+def measured_tensor_peak(sustained=False):
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["bf16_tflops_sustained" if sustained else "bf16_tflops"]), "measured"
+    return (1400.0 if sustained else 1590.0), "fallback"
+
+
+def run_prefill(args, world, rank, local):
+    """BASELINE config 5a: per GPU 8 prompts of 8192 tokens, 16 q / 2 kv heads, head_dim 256,
+    bf16 q/k/v from N(0,1).  One step = vxg_attn_cuda_q8_prefill over all 8 prompts: Q8 append
+    of every prompt token, dequantisation of the cache, causal attention on tensor cores."""
+    import torch
+    import torch.distributed as dist
+    import vxg_b200
+    K, W = args.steps, args.warmup
+    B, N, H, KV, HD = args.prompts, 8192, 16, 2, 256
+    ctx = vxg_b200.Context()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7 + rank)
+    q = torch.randn((B, N, H, HD), generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn((B, N, KV, HD), generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn((B, N, KV, HD), generator=g, device="cuda").to(torch.bfloat16)
+    pool = vxg_b200.KvQ8Pool(ctx, B, KV, HD, N)
+    seq = torch.arange(B, dtype=torch.int32, device="cuda")
+    pos = torch.zeros(B, dtype=torch.int32, device="cuda")
+    out = torch.empty((B, N, H, HD), device="cuda")
+    step = lambda: pool.prefill(seq, pos, q, k, v, out=out, max_ctx=N)
+    for _ in range(W):
+        step()
+    assert ctx.sync() == 0
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier(torch, dist, world)
+    sampler = ClockSampler(local)
+    ctx.set_timing(True)
+    sampler.start()
+    e0.record()
+    for _ in range(K):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    ms = barrier_max(torch, dist, world, e0.elapsed_time(e1))
+    attn = barrier_max(torch, dist, world, ctx.split_ms_total() / K)
+    flop = 4.0 * B * H * HD * N * (N + 1) / 2
+    peak, peak_kind = measured_tensor_peak(sustained=True)
+    ach = flop / (attn * 1e-3) / 1e12
+    res = {
+        "metric": "causal GQA prefill over the Q8 cache: prompt tokens/s and tensor TFLOP/s",
+        "value": B * N * world * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, f16 x f16 -> f32 mma",
+        "data": "synthetic",
+        "config": {"workload": f"config5a: {B} prompts x 8192 tokens per GPU, 16 q / 2 kv heads, "
+                               "head_dim 256, bf16 N(0,1) q/k/v, K/V appended to the Q8 cache",
+                   "l2": "inputs larger than L2 (1.1 GB of q/k/v/out per step)"},
+        "roofline": {"kernel": "prefill_attn_kernel", "bound": "tensor", "achieved": ach,
+                     "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                     "peak_kind": peak_kind + " (sustained bf16)",
+                     "flop_per_launch": flop, "attn_ms_per_launch": attn},
+        "gpu_launches": 3 * K, "clocks": sampler.summary(),
+    }
+    pool.close()
+    ctx.close()
+    return res
+
+
 # --------------------------------------------------------------------------- reference arm
 def run_reference(args, world, rank):
     """The reference algorithm (the C restatement of the Rust CPU operators; the Rust crate
@@ -468,10 +536,12 @@ def main():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "long", "deltanet"])
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "long", "deltanet", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seqs", type=int, default=64, help="sequences per GPU (profiling runs)")
     ap.add_argument("--ctx-max", type=int, default=32768, help="context upper bound (profiling)")
+    ap.add_argument("--prompts", type=int, default=8, help="prefill prompts per GPU (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -488,7 +558,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     try:
-        fn = {"decode": run_decode, "deltanet": run_deltanet, "long": run_long}[args.workload]
+        fn = {"decode": run_decode, "deltanet": run_deltanet, "long": run_long,
+              "prefill": run_prefill}[args.workload]
         res = fn(args, world, rank, local)
         if rank == 0:
             print(json.dumps(res), flush=True)

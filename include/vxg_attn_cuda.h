@@ -150,6 +150,28 @@ VXG_ATTN_API int vxg_attn_cuda_q8_decode_noalloc(
     const int32_t* pos, const float* q, const float* k_new, const float* v_new,
     const float* q_gate, float scale, float* out, void* stream, char* err, size_t cap);
 
+/* Chunked prefill of n_tok prompt tokens per sequence, the batched form of what the reference
+ * runs token by token (prefill_cpu_tiled, llm_prefill.rs:497-527, calling step_full_gqa_q8,
+ * :311-369) and of the Metal prefill pair vxt_cb4_gqa_prep_batch + vxt_cb4_gqa_attn_batch
+ * (native/metal_cb4_fast_run.mm:283-308): for b < n_batch, t < n_tok, the K/V of prompt token t
+ * (k_new/v_new [n_batch][n_tok][n_head_kv][head_dim]) is appended at position pos[b] + t of
+ * sequence seq_ids[b], and query token t (q [n_batch][n_tok][n_head][head_dim], prepared)
+ * attends causally to the Q8 cache [0, pos[b] + t].  q_gate (nullable, q's shape) applies
+ * out *= sigmoid(gate).  out: [n_batch][n_tok][n_head][head_dim] f32.
+ * dtype: VXG_ATTN_DTYPE_F32 or VXG_ATTN_DTYPE_BF16 for q, k_new, v_new and q_gate.
+ * Supported shapes: head_dim 64, 128 or 256, and n_head / n_head_kv dividing 128.
+ * max_ctx: an upper bound of pos[b] + n_tok (0 = the pool capacity); device scratch of
+ * 8 * n_batch * max_ctx * n_head_kv * head_dim bytes holds the dequantised cache (f16 hi and
+ * lo planes of K and V). */
+#define VXG_ATTN_DTYPE_F32 0
+#define VXG_ATTN_DTYPE_BF16 1
+VXG_ATTN_API int vxg_attn_cuda_q8_prefill(void* ctx, void* kv, uint32_t n_batch, uint32_t n_tok,
+                                          uint32_t n_head, const int32_t* seq_ids,
+                                          const int32_t* pos, const void* q, const void* k_new,
+                                          const void* v_new, const void* q_gate, int dtype,
+                                          float scale, uint32_t max_ctx, float* out, int memkind,
+                                          void* stream, char* err, size_t cap);
+
 /* Split-KV partial over tokens [kv_begin[b], kv_end[b]) of each sequence (no append): per
  * (b, head) the running max m (log2 units: max_t score_t * log2(e)), the sum
  * l = sum_t 2^(score_t*log2(e) - m) and the unnormalised o = sum_t 2^(...) * v_t.  Shapes:

@@ -159,6 +159,24 @@ def batch_decode_q8(seq_ids, pos, q, k_new, v_new, k_pool, v_pool, cap, n_head, 
     return out
 
 
+def prefill_q8(seq_ids, pos, q, k_new, v_new, k_pool, v_pool, cap, n_head, n_kv, hd,
+               scale=None, gates=None, n_threads=1):
+    """The reference's prefill attention: prompt token ti runs step_full_gqa_q8 at position
+    pos + ti, appending its K/V and attending over [0, pos + ti] (llm_prefill.rs:497-517), in
+    token order.  q [B][N][n_head][hd], k_new / v_new [B][N][n_kv][hd] f32; returns
+    out [B][N][n_head][hd]; the pools are updated in place."""
+    q, k_new, v_new = _f32(q), _f32(k_new), _f32(v_new)
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    B, N = q.shape[0], q.shape[1]
+    out = np.zeros((B, N, n_head, hd), dtype=np.float32)
+    for ti in range(N):
+        g = None if gates is None else gates[:, ti]
+        out[:, ti] = batch_decode_q8(seq_ids, pos + ti, q[:, ti], k_new[:, ti], v_new[:, ti],
+                                     k_pool, v_pool, cap, n_head, n_kv, hd, scale=scale, gates=g,
+                                     n_threads=n_threads)
+    return out
+
+
 # ---------------------------------------------------------------- gated DeltaNet (llm_ops.rs)
 def deltanet_core(q, k, v, beta_raw, alpha_raw, ssm_a, dt_bias, n_kh, n_vh, dk, dv, eps,
                   q_scale, state):

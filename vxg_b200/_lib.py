@@ -58,6 +58,8 @@ SIGNATURES = {
                                      _C, _S]),
     "vxg_attn_cuda_q8_decode_noalloc": (_I, [_P, _P, _U, _U, _U, _U, _U, _U, _P, _P, _P, _P, _P,
                                              _P, _F, _P, _P, _C, _S]),
+    "vxg_attn_cuda_q8_prefill": (_I, [_P, _P, _U, _U, _U, _P, _P, _P, _P, _P, _P, _I, _F, _U, _P,
+                                      _I, _P, _C, _S]),
     "vxg_attn_cuda_q8_decode_partial": (_I, [_P, _P, _U, _U, _P, _P, _P, _P, _F, _U, _P, _P, _P,
                                              _I, _P, _C, _S]),
     "vxg_attn_cuda_lse_combine": (_I, [_P, _U, _U, _U, _P, _P, _P, _P, _P, _I, _P, _C, _S]),

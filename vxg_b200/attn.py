@@ -55,7 +55,8 @@ class _Args:
             import torch
             if not (_is_torch(x) and x.is_cuda):
                 raise TypeError(f"{name}: expected a CUDA tensor (the call uses device memory)")
-            tdt = {np.float32: torch.float32, np.int32: torch.int32, np.uint8: torch.uint8}[dtype]
+            tdt = {np.float32: torch.float32, np.int32: torch.int32, np.uint8: torch.uint8,
+                   "bf16": torch.bfloat16}[dtype]
             if x.dtype != tdt:
                 raise TypeError(f"{name}: dtype {x.dtype}, expected {tdt}")
             if not x.is_contiguous():
@@ -65,6 +66,11 @@ class _Args:
             return ctypes.c_void_p(x.data_ptr())
         if _is_torch(x):
             raise TypeError(f"{name}: expected a numpy array (the call uses host memory)")
+        if dtype == "bf16":
+            # host bf16 travels as its raw 16-bit patterns
+            if not (isinstance(x, np.ndarray) and x.dtype == np.uint16):
+                raise TypeError(f"{name}: host bf16 data must be a uint16 numpy array of bits")
+            dtype = np.uint16
         if writable:
             if not (isinstance(x, np.ndarray) and x.dtype == dtype and x.flags.c_contiguous):
                 raise TypeError(f"{name}: must be a C-contiguous {np.dtype(dtype)} numpy array")
@@ -269,6 +275,45 @@ class KvQ8Pool:
             a.ptr(pos, np.int32, (B,), "pos"), a.ptr(q, np.float32, qshape, "q"),
             a.ptr(k_new, np.float32, kshape, "k_new"), a.ptr(v_new, np.float32, kshape, "v_new"),
             a.ptr(q_gate, np.float32, qshape, "q_gate"), ctypes.c_float(scale), max_ctx,
+            a.ptr(out, np.float32, qshape, "out", writable=True), a.memkind, a.stream(stream),
+            err.buf, err.cap), err)
+        self.last_rc = rc
+        return out
+
+    def prefill(self, seq_ids, pos, q, k_new, v_new, q_gate=None, scale=None,
+                max_ctx: int = 0, out=None, stream=None):
+        """Append the prompt's K/V at pos[b] + t and attend each query token causally.
+
+        q [B][n_tok][n_head][head_dim] and k_new / v_new [B][n_tok][n_head_kv][head_dim] are f32
+        or bf16 (torch.bfloat16 on the device, uint16 bit patterns on the host).
+        Returns out [B][n_tok][n_head][head_dim] f32."""
+        a = _Args(q)
+        if a.device:
+            import torch
+            bf16 = q.dtype == torch.bfloat16
+        else:
+            bf16 = isinstance(q, np.ndarray) and q.dtype == np.uint16
+        dt = "bf16" if bf16 else np.float32
+        B = len(seq_ids) if not a.device else seq_ids.numel()
+        kv_el = (k_new.size if not a.device else k_new.numel())
+        n_tok = kv_el // (B * self.n_head_kv * self.head_dim)
+        n_head = (q.size if not a.device else q.numel()) // (B * n_tok * self.head_dim)
+        qshape = (B, n_tok, n_head, self.head_dim)
+        kshape = (B, n_tok, self.n_head_kv, self.head_dim)
+        if scale is None:
+            scale = 1.0 / math.sqrt(self.head_dim)
+        if out is None:
+            if a.device:
+                import torch
+                out = torch.empty(qshape, dtype=torch.float32, device=q.device)
+            else:
+                out = np.empty(qshape, np.float32)
+        err = ErrBuf()
+        rc = check(lib().vxg_attn_cuda_q8_prefill(
+            self.ctx.h, self.h, B, n_tok, n_head, a.ptr(seq_ids, np.int32, (B,), "seq_ids"),
+            a.ptr(pos, np.int32, (B,), "pos"), a.ptr(q, dt, qshape, "q"),
+            a.ptr(k_new, dt, kshape, "k_new"), a.ptr(v_new, dt, kshape, "v_new"),
+            a.ptr(q_gate, dt, qshape, "q_gate"), int(bf16), ctypes.c_float(scale), max_ctx,
             a.ptr(out, np.float32, qshape, "out", writable=True), a.memkind, a.stream(stream),
             err.buf, err.cap), err)
         self.last_rc = rc

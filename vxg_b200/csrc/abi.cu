@@ -82,6 +82,7 @@ struct Ctx {
   DevBuf io;                    // device staging for host-memory calls
   DevBuf aux;                   // prepared q / gate / rope table for the drop-in step
   DevBuf aux2;                  // DeltaNet scratch (conv output, normalised q/k, gates)
+  DevBuf pre;                   // prefill: dequantised f16 cache
   std::set<struct Kv*> pools;   // KV pools created on this context (orphaned on destroy)
 };
 
@@ -322,6 +323,7 @@ void vxg_attn_cuda_destroy(void* h) {
   c->io.release();
   c->aux.release();
   c->aux2.release();
+  c->pre.release();
   if (c->d_status) cudaFree(c->d_status);
   if (c->h_status) cudaFreeHost(c->h_status);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -629,6 +631,78 @@ int vxg_attn_cuda_q8_decode(void* ctx, void* h, uint32_t n_batch, uint32_t n_hea
     record_timing(c, &e0, &e1);
     check(vxg::launch_decode(a, p, q_gate, out, c.sm_count, c.force_generic, st, e0, e1),
           "decode launch");
+    sg.download();
+    return finish(c, stream, st);
+  });
+}
+
+int vxg_attn_cuda_q8_prefill(void* ctx, void* h, uint32_t n_batch, uint32_t n_tok,
+                             uint32_t n_head, const int32_t* seq_ids, const int32_t* pos,
+                             const void* q, const void* k_new, const void* v_new,
+                             const void* q_gate, int dtype, float scale, uint32_t max_ctx,
+                             float* out, int memkind, void* stream, char* err, size_t cap) {
+  return guarded(ctx, stream, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    Kv& kv = use_kv(c, h);
+    if (n_batch == 0 || n_tok == 0) return VXG_ATTN_OK;
+    require(seq_ids && pos && q && k_new && v_new && out, VXG_ATTN_ERR_NULL_PTR, "null input");
+    require(dtype == VXG_ATTN_DTYPE_F32 || dtype == VXG_ATTN_DTYPE_BF16,
+            VXG_ATTN_ERR_INVALID_OPTION, "dtype must be VXG_ATTN_DTYPE_F32 or _BF16");
+    check_decode_shape(kv, n_batch, n_head);
+    require(vxg::prefill_supported((int)n_head, (int)kv.n_kv, (int)kv.hd),
+            VXG_ATTN_ERR_UNSUPPORTED,
+            "prefill needs head_dim 64/128/256 and n_head/n_head_kv dividing 128");
+    require((uint64_t)n_tok * (n_head / kv.n_kv) <= 65535ull * 128, VXG_ATTN_ERR_INVALID_OPTION,
+            "n_tok too large for one prefill call");
+    require(n_tok <= kv.cap, VXG_ATTN_ERR_BUFFER_TOO_SMALL, "n_tok beyond the KV capacity");
+    const uint32_t lmax = (max_ctx == 0 || max_ctx > kv.cap) ? kv.cap : max_ctx;
+    require(n_tok <= lmax, VXG_ATTN_ERR_INVALID_OPTION, "max_ctx below n_tok");
+    const bool host = memkind == VXG_ATTN_MEM_HOST;
+    if (host) {
+      check_host_positions(kv, n_batch, seq_ids, pos, n_tok);
+      for (uint32_t b = 0; b < n_batch; ++b)
+        require((uint64_t)pos[b] + n_tok <= lmax, VXG_ATTN_ERR_INVALID_OPTION,
+                "pos + n_tok beyond max_ctx");
+    }
+    cudaStream_t st = pick_stream(c, stream);
+    const size_t es = dtype == VXG_ATTN_DTYPE_BF16 ? 2 : 4;
+    const size_t bt = (size_t)n_batch * n_tok;
+    const size_t qb = bt * n_head * kv.hd * es;
+    const size_t kvd = bt * kv.n_kv * kv.hd * es;
+    Stager sg(c, st, host);
+    sg.in(seq_ids, n_batch * sizeof(int32_t));
+    sg.in(pos, n_batch * sizeof(int32_t));
+    sg.in(q, qb);
+    sg.in(k_new, kvd);
+    sg.in(v_new, kvd);
+    sg.in(q_gate, qb);
+    sg.out(out, bt * n_head * kv.hd * sizeof(float));
+    sg.upload();
+    vxg::PrefillArgs a{};
+    a.seq_ids = seq_ids;
+    a.pos_base = pos;
+    a.q = q;
+    a.k_new = k_new;
+    a.v_new = v_new;
+    a.gate = q_gate;
+    a.k_pool = kv.k;
+    a.v_pool = kv.v;
+    a.out = out;
+    a.n_batch = (int)n_batch;
+    a.n_tok = (int)n_tok;
+    a.n_seq = (int)kv.n_seq;
+    a.cap = (int)kv.cap;
+    a.n_head = (int)n_head;
+    a.n_kv = (int)kv.n_kv;
+    a.hd = (int)kv.hd;
+    a.lmax = (int)lmax;
+    a.scale = scale;
+    a.status = c.d_status;
+    c.pre.reserve(vxg::prefill_scratch_bytes(a), "cudaMalloc prefill scratch");
+    cudaEvent_t e0, e1;
+    record_timing(c, &e0, &e1);
+    check(vxg::launch_prefill(a, c.pre.p, dtype == VXG_ATTN_DTYPE_BF16, st, e0, e1),
+          "prefill launch");
     sg.download();
     return finish(c, stream, st);
   });

@@ -1,5 +1,6 @@
 // Shared device helpers for the sm_100a Q8-KV attention / gated-DeltaNet backend.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>

@@ -11,6 +11,11 @@ cudaError_t launch_q8_append(const int32_t* seq_ids, const int32_t* pos, const f
                              const float* v_new, uint8_t* k_pool, uint8_t* v_pool, int n_batch,
                              int n_tok, int n_seq, int cap, int n_kv, int nb, uint32_t* status,
                              cudaStream_t stream);
+// Same with bf16 inputs (k_new / v_new are __nv_bfloat16; bf16 -> f32 is exact).
+cudaError_t launch_q8_append_bf16(const int32_t* seq_ids, const int32_t* pos, const void* k_new,
+                                  const void* v_new, uint8_t* k_pool, uint8_t* v_pool, int n_batch,
+                                  int n_tok, int n_seq, int cap, int n_kv, int nb, uint32_t* status,
+                                  cudaStream_t stream);
 
 // decode_attn.cu ---------------------------------------------------------------------------
 struct DecodeArgs {
@@ -89,6 +94,32 @@ cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, cudaSt
 // conv1d + SiLU over the rolling history (llm_ops.rs:122-137), batched.
 cudaError_t launch_deltanet_conv(const float* x, const float* w, float* conv_state, float* out,
                                  int n_batch, int conv_ch, int k_sz, cudaStream_t stream);
+
+// prefill_attn.cu --------------------------------------------------------------------------
+struct PrefillArgs {
+  const int32_t* seq_ids;  // [n_batch]
+  const int32_t* pos_base; // [n_batch] cache position of prompt token 0
+  const void* q;           // [n_batch][n_tok][n_head][hd] (f32 or bf16) prepared queries
+  const void* k_new;       // [n_batch][n_tok][n_kv][hd] appended to the cache first
+  const void* v_new;
+  const void* gate;        // optional sigmoid gate, q's shape and type
+  const uint8_t* k_pool;   // [n_seq][cap][n_kv][hd/32] blocks (written by the append)
+  const uint8_t* v_pool;
+  float* out;              // [n_batch][n_tok][n_head][hd]
+  __half* kd[2];           // dequantised cache, hi and lo f16 planes [n_batch][lmax][n_kv][hd]
+  __half* vd[2];           // (carved from scratch by launch_prefill)
+  int n_batch, n_tok, n_seq, cap, n_head, n_kv, hd;
+  int lmax;                // >= pos_base[b] + n_tok for every b (host-known)
+  float scale;
+  uint32_t* status;
+};
+// Append + causal attention of n_tok prompt tokens per sequence (hd = 256, n_head = 8 * n_kv).
+size_t prefill_scratch_bytes(const PrefillArgs& a);
+size_t prefill_smem_bytes();
+bool prefill_supported(int n_head, int n_kv, int hd);
+// ev_attn_begin / ev_attn_end (nullable) bracket the attention kernel.
+cudaError_t launch_prefill(const PrefillArgs& a, void* scratch, int bf16, cudaStream_t stream,
+                           cudaEvent_t ev_attn_begin, cudaEvent_t ev_attn_end);
 
 // prep.cu ----------------------------------------------------------------------------------
 // q/k prologue of step_full_gqa_q8 for one token: rope_cs = host-computed (cos, sin) pairs.

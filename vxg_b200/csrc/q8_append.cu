@@ -12,10 +12,15 @@
 
 namespace vxg {
 
+__device__ __forceinline__ float load_f32(const float* p) { return *p; }
+__device__ __forceinline__ float load_f32(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+// T = float or __nv_bfloat16 (bf16 widens to f32 exactly, so the codes are those of the f32 value)
+template <typename T>
 __global__ void __launch_bounds__(256) q8_append_kernel(const int32_t* __restrict__ seq_ids,
                                                          const int32_t* __restrict__ pos,
-                                                         const float* __restrict__ k_new,
-                                                         const float* __restrict__ v_new,
+                                                         const T* __restrict__ k_new,
+                                                         const T* __restrict__ v_new,
                                                          uint8_t* __restrict__ k_pool,
                                                          uint8_t* __restrict__ v_pool,
                                                          int n_batch, int n_tok, int n_seq,
@@ -38,8 +43,8 @@ __global__ void __launch_bounds__(256) q8_append_kernel(const int32_t* __restric
     if (lane == 0) atomicOr(status, kStatusBadIndex);
     return;
   }
-  const float* src = (which ? v_new : k_new) + ((size_t)bt * per_tok + blk) * 32;
-  const float x = src[lane];
+  const T* src = (which ? v_new : k_new) + ((size_t)bt * per_tok + blk) * 32;
+  const float x = load_f32(src + lane);
   // amax starts at 0 and ignores NaN (f32::max); fmaxf(0, NaN) = 0 gives the same.
   const float amax = warp_max(fmaxf(0.0f, fabsf(x)));
   const uint16_t dh = f32_to_f16bits(amax / 127.0f);
@@ -60,8 +65,23 @@ cudaError_t launch_q8_append(const int32_t* seq_ids, const int32_t* pos, const f
   if (warps == 0) return cudaSuccess;
   const int threads = 256;
   const long long blocks = (warps * 32 + threads - 1) / threads;
-  q8_append_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
+  q8_append_kernel<float><<<(unsigned)blocks, threads, 0, stream>>>(
       seq_ids, pos, k_new, v_new, k_pool, v_pool, n_batch, n_tok, n_seq, cap, n_kv, nb, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_q8_append_bf16(const int32_t* seq_ids, const int32_t* pos, const void* k_new,
+                                  const void* v_new, uint8_t* k_pool, uint8_t* v_pool, int n_batch,
+                                  int n_tok, int n_seq, int cap, int n_kv, int nb, uint32_t* status,
+                                  cudaStream_t stream) {
+  const long long warps = 2LL * n_batch * n_tok * n_kv * nb;
+  if (warps == 0) return cudaSuccess;
+  const int threads = 256;
+  const long long blocks = (warps * 32 + threads - 1) / threads;
+  q8_append_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, stream>>>(
+      seq_ids, pos, static_cast<const __nv_bfloat16*>(k_new),
+      static_cast<const __nv_bfloat16*>(v_new), k_pool, v_pool, n_batch, n_tok, n_seq, cap, n_kv,
+      nb, status);
   return cudaGetLastError();
 }
 
