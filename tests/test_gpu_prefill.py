@@ -43,7 +43,7 @@ def _prefilled_pools(ctx, rng, n_seq, n_kv, hd, cap, prior):
 
 
 def _run_case(ctx, rng, n_head, n_kv, hd, prior, seq, n_tok, gated=False, bf16=False,
-              device=False, cap=None):
+              device=False, cap=None, generic=False):
     n_seq = len(prior)
     B = len(seq)
     cap = cap or (max(prior) + n_tok + 3)
@@ -62,6 +62,7 @@ def _run_case(ctx, rng, n_head, n_kv, hd, prior, seq, n_tok, gated=False, bf16=F
         args = (qb, kb, vb, gb)
     else:
         args = (q, k, v, g)
+    ctx.force_generic(generic)
     if device:
         import torch
 
@@ -78,6 +79,7 @@ def _run_case(ctx, rng, n_head, n_kv, hd, prior, seq, n_tok, gated=False, bf16=F
     else:
         out = pool.prefill(seq, pos, *args[:3], q_gate=args[3])
         assert pool.last_rc == 0
+    ctx.force_generic(False)
     want = oracle.prefill_q8(seq, pos, q, k, v, kh.reshape(-1), vh.reshape(-1), cap, n_head,
                              n_kv, hd, gates=g, n_threads=8)
     np.testing.assert_allclose(out, want, atol=ATOL, rtol=RTOL)
@@ -99,10 +101,26 @@ def test_prefill_f32_host_ragged(ctx):
     assert ratio.max() < 0.02
 
 
-def test_prefill_bf16_device_gated(ctx):
+@pytest.mark.parametrize("generic", [False, True])
+def test_prefill_bf16_device_gated(ctx, generic):
+    """bf16 inputs: the tcgen05/TMEM kernel (generic=False) and the mma.sync kernel."""
     rng = np.random.default_rng(51)
-    _run_case(ctx, rng, 16, 2, 256, prior=[5, 64], seq=[1, 0], n_tok=97, gated=True, bf16=True,
-              device=True)
+    out, want = _run_case(ctx, rng, 16, 2, 256, prior=[5, 64], seq=[1, 0], n_tok=97, gated=True,
+                          bf16=True, device=True, generic=generic)
+    ratio = np.abs(out - want) / (ATOL + RTOL * np.abs(want))
+    assert ratio.max() < 0.02
+
+
+@pytest.mark.parametrize("n_head,n_kv", [(16, 2), (32, 2), (8, 2), (4, 4)])
+def test_prefill_bf16_tensor_memory_kernel(ctx, n_head, n_kv):
+    """The tcgen05 kernel at head_dim 256 over query groups of 16, 8, 4 and 1 heads per kv head,
+    prompts continuing cached contexts (0, 33 and 300 tokens; n_tok not a multiple of the
+    query block or the 32-key tile)."""
+    rng = np.random.default_rng(57 + n_head)
+    out, want = _run_case(ctx, rng, n_head, n_kv, 256, prior=[33, 0, 300], seq=[2, 1, 0],
+                          n_tok=75, bf16=True, device=True)
+    ratio = np.abs(out - want) / (ATOL + RTOL * np.abs(want))
+    assert ratio.max() < 0.02
 
 
 @pytest.mark.parametrize("n_head,n_kv,hd", [(8, 2, 128), (4, 4, 64), (32, 2, 128), (4, 1, 256)])

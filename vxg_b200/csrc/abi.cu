@@ -698,11 +698,13 @@ int vxg_attn_cuda_q8_prefill(void* ctx, void* h, uint32_t n_batch, uint32_t n_to
     a.lmax = (int)lmax;
     a.scale = scale;
     a.status = c.d_status;
-    c.pre.reserve(vxg::prefill_scratch_bytes(a), "cudaMalloc prefill scratch");
+    const int bf16 = dtype == VXG_ATTN_DTYPE_BF16;
+    const int allow_tc = !c.force_generic;
+    if (!(allow_tc && vxg::prefill_tc_supported((int)n_head, (int)kv.n_kv, (int)kv.hd, bf16)))
+      c.pre.reserve(vxg::prefill_scratch_bytes(a), "cudaMalloc prefill scratch");
     cudaEvent_t e0, e1;
     record_timing(c, &e0, &e1);
-    check(vxg::launch_prefill(a, c.pre.p, dtype == VXG_ATTN_DTYPE_BF16, st, e0, e1),
-          "prefill launch");
+    check(vxg::launch_prefill(a, c.pre.p, bf16, allow_tc, st, e0, e1), "prefill launch");
     sg.download();
     return finish(c, stream, st);
   });

@@ -117,9 +117,16 @@ struct PrefillArgs {
 size_t prefill_scratch_bytes(const PrefillArgs& a);
 size_t prefill_smem_bytes();
 bool prefill_supported(int n_head, int n_kv, int hd);
-// ev_attn_begin / ev_attn_end (nullable) bracket the attention kernel.
-cudaError_t launch_prefill(const PrefillArgs& a, void* scratch, int bf16, cudaStream_t stream,
-                           cudaEvent_t ev_attn_begin, cudaEvent_t ev_attn_end);
+// ev_attn_begin / ev_attn_end (nullable) bracket the attention kernel.  With allow_tc, bf16
+// inputs at head_dim 256 run the tcgen05/TMEM kernel (prefill_tc.cu, no scratch used); everything
+// else runs the mma.sync kernel over the dequantised f16 planes.
+cudaError_t launch_prefill(const PrefillArgs& a, void* scratch, int bf16, int allow_tc,
+                           cudaStream_t stream, cudaEvent_t ev_attn_begin,
+                           cudaEvent_t ev_attn_end);
+// prefill_tc.cu
+bool prefill_tc_supported(int n_head, int n_kv, int hd, int bf16);
+size_t prefill_tc_smem_bytes();
+cudaError_t launch_prefill_tc(const PrefillArgs& a, cudaStream_t stream);
 
 // prep.cu ----------------------------------------------------------------------------------
 // q/k prologue of step_full_gqa_q8 for one token: rope_cs = host-computed (cos, sin) pairs.

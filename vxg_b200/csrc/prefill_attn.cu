@@ -383,11 +383,12 @@ bool prefill_supported(int n_head, int n_kv, int hd) {
   return (hd == 64 || hd == 128 || hd == 256) && g >= 1 && pf::ROWS % g == 0;
 }
 
-cudaError_t launch_prefill(const PrefillArgs& a0, void* scratch, int bf16, cudaStream_t st,
-                           cudaEvent_t ev0, cudaEvent_t ev1) {
+cudaError_t launch_prefill(const PrefillArgs& a0, void* scratch, int bf16, int allow_tc,
+                           cudaStream_t st, cudaEvent_t ev0, cudaEvent_t ev1) {
   PrefillArgs a = a0;
   if (a.n_batch == 0 || a.n_tok == 0) return cudaSuccess;
   if (!prefill_supported(a.n_head, a.n_kv, a.hd)) return cudaErrorInvalidValue;
+  const bool tcpath = allow_tc && prefill_tc_supported(a.n_head, a.n_kv, a.hd, bf16);
   // four 256-byte aligned planes: K hi, K lo, V hi, V lo
   const size_t plane = ((size_t)a.n_batch * a.lmax * a.n_kv * a.hd * sizeof(__half) + 255) &
                        ~size_t(255);
@@ -406,6 +407,13 @@ cudaError_t launch_prefill(const PrefillArgs& a0, void* scratch, int bf16, cudaS
                               static_cast<const float*>(a.v_new), kp, vp, a.n_batch, a.n_tok,
                               a.n_seq, a.cap, a.n_kv, a.hd / 32, a.status, st);
   if (e != cudaSuccess) return e;
+  if (tcpath) {
+    // tensor-memory kernel: dequantises the Q8 records on chip
+    if (ev0) cudaEventRecord(ev0, st);
+    e = launch_prefill_tc(a, st);
+    if (ev1) cudaEventRecord(ev1, st);
+    return e;
+  }
   // 2. dequantise [0, pos_base + n_tok) into the f16 hi/lo planes
   const long long chunks = (long long)a.n_batch * a.lmax * a.n_kv * a.hd / 8;
   q8_dequant_f16_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(a);
