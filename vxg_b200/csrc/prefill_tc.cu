@@ -5,22 +5,25 @@
 //
 // One CTA = 128 query rows (128 / G prompt tokens x the G query heads of one kv head), keys in
 // tiles of 32, 16 warps with fixed roles:
-//   warp 0       loader: 1-D bulk copies of the tile's Q8 records (272 B per key and cache) from
-//                the KV pool into a 3-deep raw ring;
+//   warp 0       loader: one 2-D TMA tensor copy per cache and tile (this kv head's 272-byte
+//                Q8 records of 32 tokens) from the KV pool into a 3-deep raw ring;
 //   warp 1       MMA issuer (one thread) and TMEM owner;
 //   warps 4-7    softmax: thread = query row = TMEM lane; also Q -> TMEM and the epilogue;
 //   warps 8-15   converters: Q8 records -> f16 hi/lo planes (K and V) in 128-byte-swizzled
 //                shared memory, double-buffered separately for K and V.
-// Tensor memory (512 columns): O [0,256) f32, Q [256,384) f16 pairs, S0/S1 [384,448) f32.  The
-// softmax writes P (f16 hi and lo halves) over its S buffer; both MMAs take A from TMEM:
-//   S  = Q Kh^T + Q Kl^T                          (kind::f16, M=128, N=32, 2 x 16 K-steps)
+// Tensor memory (512 columns): O [0,256) f32, Q [256,384) f16 pairs, S0/S1 [384,512) f32.  The
+// K hi and lo planes are stacked as 64 B-rows, so one MMA per K-step gives both halves of S:
+//   [S_hi | S_lo] = Q [Kh ; Kl]^T                 (kind::f16, M=128, N=64, 16 K-steps)
 //   O += Ph Vh + Ph Vl + Pl Vh                    (kind::f16, M=128, N=256, 3 x 2 K-steps)
+// and the softmax reads S = S_hi + S_lo, then writes P (f16 hi and lo halves) over its S buffer;
+// both MMAs take A from TMEM.
 // bf16 queries are exact in f16, and Kh+Kl, Vh+Vl reproduce code*d exactly, so the products
 // match the fp32 reference to ~2^-22 relative plus f32 accumulation rounding.
 // The running max used as exponent base is only moved when a tile's max exceeds it by more
 // than 8 (log2 units); P then stays <= 256, and O (in TMEM) is rescaled only on those moves.
 // Every wait is bounded in wall-clock time; a wait that gives up raises the CTA's abort flag and
 // the status word, and all roles leave their loops.
+#include <cuda.h>
 #include <cuda_bf16.h>
 
 #include "kernels.h"
@@ -36,13 +39,13 @@ constexpr int NRAW = 3;           // raw Q8 ring depth
 constexpr int REC = 272;          // bytes of one key's blocks for one kv head (8 x 34)
 constexpr int THREADS = 512;
 constexpr int PLANE = KT * 2 * HD;            // bytes of one f16 plane tile (16 KB)
-constexpr uint32_t TM_O = 0, TM_Q = 256, TM_S = 384;
+constexpr uint32_t TM_O = 0, TM_Q = 256, TM_S = 384;  // S buffers: 64 columns each
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr float kRescale = 8.0f;  // log2 units
 
 struct __align__(1024) Smem {
-  uint8_t kpl[2][2][PLANE];       // [stage][hi/lo]: [dim/64 (4)][key (32)][128 B] swizzled
-  uint8_t vpl[2][2][PLANE];
+  uint8_t kpl[2][2 * PLANE];      // [stage]: [dim/64 (4)][row (64): Kh keys, then Kl][128 B]
+  uint8_t vpl[2][2][PLANE];       // [stage][hi/lo]: [dim/64 (4)][key (32)][128 B]
   uint8_t raw[NRAW][2][KT * REC]; // [stage][K/V][key][272 B]
   uint64_t raw_full[NRAW], raw_empty[NRAW];
   uint64_t kf[2], ke[2], vf[2], ve[2];
@@ -80,6 +83,16 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Sm
   }
 }
 
+// 2-D tiled tensor copy global -> shared completing on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
@@ -87,8 +100,13 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 
 // One (key, 32-dim block) item: 34-byte Q8 block at `blk` (2-byte aligned) -> 32 f16 values of
 // the hi plane and 32 of the lo plane, written as 4 swizzled 16-byte chunks each.
+// All arithmetic is f16x2 and exact where it has to be: the codes become f16 exactly
+// (byte ^ 0x80 under the 0x64 exponent is 1024 + code + 128), hi = RN(code * d) is one rounded
+// multiply, and lo = RN(code * d - hi) is one fused multiply-add whose result is exact (the
+// residual has at most 8 significant bits).
 __device__ __forceinline__ void convert_block(const uint8_t* blk, uint8_t* hi_plane,
-                                              uint8_t* lo_plane, int key, int c, bool valid) {
+                                              uint8_t* lo_plane, uint32_t atom_stride, int key,
+                                              int c, bool valid) {
   uint32_t a[9];
   if (valid) {
     const uint32_t* wb =
@@ -104,25 +122,26 @@ __device__ __forceinline__ void convert_block(const uint8_t* blk, uint8_t* hi_pl
 #pragma unroll
     for (int i = 0; i < 9; ++i) a[i] = 0u;
   }
-  const float d = f16bits_to_f32((uint16_t)(a[0] & 0xFFFFu));
-  // code k sits in byte (k + 2) of the aligned stream a[]
-  auto code = [&](int k) -> float {
-    const int byte = k + 2;
-    return (float)(int8_t)((a[byte >> 2] >> ((byte & 3) * 8)) & 0xFFu);
-  };
+  // a[0]: scale bits (low half), codes 0-1 (high half); a[i]: codes 4i-2 .. 4i+1
+  const uint32_t d2u = __byte_perm(a[0], 0u, 0x1010);
+  const __half2 d2 = *reinterpret_cast<const __half2*>(&d2u);
+  const __half2 bias = __floats2half2_rn(1152.f, 1152.f);
   const int atom = c >> 1;
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
     uint32_t h[4], l[4];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const float x0 = code(8 * m + 2 * p) * d, x1 = code(8 * m + 2 * p + 1) * d;  // exact
-      const __half2 hh = __floats2half2_rn(x0, x1);
-      const float2 hf = __half22float2(hh);
-      h[p] = *reinterpret_cast<const uint32_t*>(&hh);
-      l[p] = pack_h2(x0 - hf.x, x1 - hf.y);
+    for (int q = 0; q < 4; ++q) {
+      const int p = 4 * m + q;  // codes 2p, 2p+1 sit in bytes 2p+2, 2p+3 of the stream
+      const uint32_t w = a[(p + 1) >> 1] ^ 0x80808080u;
+      const uint32_t bu = __byte_perm(w, 0x64646464u, ((p + 1) & 1) ? 0x4342 : 0x4140);
+      const __half2 code = __hsub2(*reinterpret_cast<const __half2*>(&bu), bias);  // exact
+      const __half2 hi = __hmul2(code, d2);
+      const __half2 lo = __hfma2(code, d2, __hneg2(hi));
+      h[q] = *reinterpret_cast<const uint32_t*>(&hi);
+      l[q] = *reinterpret_cast<const uint32_t*>(&lo);
     }
-    const uint32_t off = atom * (KT * 128) + tc::sw128_off(key, (c & 1) * 4 + m);
+    const uint32_t off = atom * atom_stride + tc::sw128_off(key, (c & 1) * 4 + m);
     *reinterpret_cast<uint4*>(hi_plane + off) = make_uint4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<uint4*>(lo_plane + off) = make_uint4(l[0], l[1], l[2], l[3]);
   }
@@ -130,7 +149,11 @@ __device__ __forceinline__ void convert_block(const uint8_t* blk, uint8_t* hi_pl
 
 }  // namespace pftc
 
-__global__ void __launch_bounds__(pftc::THREADS, 1) prefill_tc_kernel(PrefillArgs a) {
+// kmap / vmap: the K and V pools as 2-D u32 tensors [n_seq * cap rows][token bytes / 4], box
+// 68 x 32 (one kv head's 272 bytes of 32 tokens).
+__global__ void __launch_bounds__(pftc::THREADS, 1)
+    prefill_tc_kernel(PrefillArgs a, const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap) {
   using namespace pftc;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
@@ -192,25 +215,24 @@ __global__ void __launch_bounds__(pftc::THREADS, 1) prefill_tc_kernel(PrefillArg
 
   if (warp == 0) {
     // ---------------------------------------------------------------- loader
-    const size_t rec_stride = (size_t)a.n_kv * nb * kBlk;  // bytes per token in one cache
-    const uint8_t* kseq = a.k_pool + (size_t)s * a.cap * rec_stride + (size_t)kh * REC;
-    const uint8_t* vseq = a.v_pool + (size_t)s * a.cap * rec_stride + (size_t)kh * REC;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int rs = j % NRAW;
-      if (j >= NRAW && !wait_or_abort(&sm.raw_empty[rs], ((j / NRAW) - 1) & 1, sm, status)) break;
-      const int nv = min(KT, key_end - j * KT);
-      if (lane == 0) mbar_arrive_expect_tx(&sm.raw_full[rs], (uint32_t)(nv * 2 * REC));
-      __syncwarp();
-      if (lane < nv) {
-        const size_t off = (size_t)(j * KT + lane) * rec_stride;
-        bulk_g2s(sm.raw[rs][0] + lane * REC, kseq + off, REC, &sm.raw_full[rs]);
-        bulk_g2s(sm.raw[rs][1] + lane * REC, vseq + off, REC, &sm.raw_full[rs]);
+    if (lane == 0) {
+      const int row0 = s * a.cap;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int rs = j % NRAW;
+        if (j >= NRAW && !wait_or_abort(&sm.raw_empty[rs], ((j / NRAW) - 1) & 1, sm, status))
+          break;
+        // whole boxes always land (rows past the sequence are other tokens or zero fill; the
+        // converters ignore keys >= key_end)
+        mbar_arrive_expect_tx(&sm.raw_full[rs], (uint32_t)(2 * KT * REC));
+        tma_load_2d(sm.raw[rs][0], &kmap, kh * (REC / 4), row0 + j * KT, &sm.raw_full[rs]);
+        tma_load_2d(sm.raw[rs][1], &vmap, kh * (REC / 4), row0 + j * KT, &sm.raw_full[rs]);
       }
     }
+    __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t id_qk = tc::idesc_f16(128, KT, false);
+      const uint32_t id_qk = tc::idesc_f16(128, 2 * KT, false);
       const uint32_t id_pv = tc::idesc_f16(128, HD, true);
       bool ok = wait_or_abort(&sm.q_full, 0, sm, status);
       tc::fence_after_sync();
@@ -219,7 +241,7 @@ __global__ void __launch_bounds__(pftc::THREADS, 1) prefill_tc_kernel(PrefillArg
         if (!wait_or_abort(&sm.vf[st], (i >> 1) & 1, sm, status)) return false;
         if (!wait_or_abort(&sm.p_full[st], (i >> 1) & 1, sm, status)) return false;
         tc::fence_after_sync();
-        const uint32_t ph = tm + TM_S + 32 * st, pl = ph + 16;
+        const uint32_t ph = tm + TM_S + 2 * KT * st, pl = ph + 16;
         const uint32_t vh = smem_u32(sm.vpl[st][0]), vl = smem_u32(sm.vpl[st][1]);
 #pragma unroll
         for (int kk = 0; kk < KT / 16; ++kk) {
@@ -238,18 +260,13 @@ __global__ void __launch_bounds__(pftc::THREADS, 1) prefill_tc_kernel(PrefillArg
         const int st = j & 1;
         if (!wait_or_abort(&sm.kf[st], (j >> 1) & 1, sm, status)) { ok = false; break; }
         tc::fence_after_sync();
-        const uint32_t kh_s = smem_u32(sm.kpl[st][0]), kl_s = smem_u32(sm.kpl[st][1]);
-        const uint32_t sd = tm + TM_S + 32 * st;
+        const uint32_t k_s = smem_u32(sm.kpl[st]);
+        const uint32_t sd = tm + TM_S + 2 * KT * st;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * (KT * 128) + (kk & 3) * 32;
-          tc::mma_ts(sd, tm + TM_Q + kk * 8, tc::sdesc_sw128(kh_s + koff, 16, 1024), id_qk,
+          const uint32_t koff = (kk >> 2) * (2 * KT * 128) + (kk & 3) * 32;
+          tc::mma_ts(sd, tm + TM_Q + kk * 8, tc::sdesc_sw128(k_s + koff, 16, 1024), id_qk,
                      kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * (KT * 128) + (kk & 3) * 32;
-          tc::mma_ts(sd, tm + TM_Q + kk * 8, tc::sdesc_sw128(kl_s + koff, 16, 1024), id_qk, 1u);
         }
         tc::mma_commit(&sm.ke[st]);
         tc::mma_commit(&sm.s_full[st]);
@@ -305,15 +322,16 @@ __global__ void __launch_bounds__(pftc::THREADS, 1) prefill_tc_kernel(PrefillArg
       if (!wait_or_abort(&sm.s_full[st], (j >> 1) & 1, sm, status)) { ok = false; break; }
       __syncwarp();
       tc::fence_after_sync();
-      uint32_t sv[32];
-      tc::tmem_ld32(lane_addr + TM_S + 32 * st, sv);
+      uint32_t sv[32], sl[32];
+      tc::tmem_ld32(lane_addr + TM_S + 2 * KT * st, sv);       // Q Kh^T
+      tc::tmem_ld32(lane_addr + TM_S + 2 * KT * st + KT, sl);  // Q Kl^T
       tc::wait_ld();
       float x[32];
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
         const int key = j * KT + c;
-        x[c] = key <= qpos ? __uint_as_float(sv[c]) * sl2 : -INFINITY;
+        x[c] = key <= qpos ? (__uint_as_float(sv[c]) + __uint_as_float(sl[c])) * sl2 : -INFINITY;
         mx = fmaxf(mx, x[c]);
       }
       const bool move = mx > m_used + kRescale;
@@ -351,8 +369,8 @@ __global__ void __launch_bounds__(pftc::THREADS, 1) prefill_tc_kernel(PrefillArg
         pl[c] = pack_h2(p0 - hf.x, p1 - hf.y);
       }
       l += ps;
-      tc::tmem_st16(lane_addr + TM_S + 32 * st, ph);
-      tc::tmem_st16(lane_addr + TM_S + 32 * st + 16, pl);
+      tc::tmem_st16(lane_addr + TM_S + 2 * KT * st, ph);
+      tc::tmem_st16(lane_addr + TM_S + 2 * KT * st + 16, pl);
       tc::wait_st();
       tc::fence_before_sync();
       tc::mbar_arrive(&sm.p_full[st]);
@@ -392,22 +410,28 @@ __global__ void __launch_bounds__(pftc::THREADS, 1) prefill_tc_kernel(PrefillArg
     }
   } else if (warp >= 8) {
     // ---------------------------------------------------------------- converters
-    const int c = warp - 8;  // 32-dim block handled by this warp; lane = key of the tile
+    // Lane -> (key, 32-dim block): 8 keys x blocks {0,2,4,6} (warps 8-11) or {1,3,5,7}
+    // (warps 12-15).  Record rows are 68 words apart, so 8 keys start in 8 banks = 0 mod 4, and
+    // those four blocks start at word offsets 0, 1, 2, 3 mod 4: the 32 lanes read 32 distinct
+    // banks, and the swizzled 16-byte stores of 8 keys cover all banks once per block.
+    const int wc = warp - 8;
+    const int key = 8 * (wc & 3) + (lane & 7);
+    const int c = 2 * (lane >> 3) + (wc >> 2);
     for (int j = 0; j < n_tiles; ++j) {
       const int rs = j % NRAW, st = j & 1;
       if (!wait_or_abort(&sm.raw_full[rs], (j / NRAW) & 1, sm, status)) break;
-      const bool valid = j * KT + lane < key_end;
+      const bool valid = j * KT + key < key_end;
       // K planes of stage st are free once QK of tile j-2 is done
       if (j >= 2 && !wait_or_abort(&sm.ke[st], ((j >> 1) - 1) & 1, sm, status)) break;
-      pftc::convert_block(sm.raw[rs][0] + lane * REC + c * kBlk, sm.kpl[st][0], sm.kpl[st][1],
-                          lane, c, valid);
+      pftc::convert_block(sm.raw[rs][0] + key * REC + c * kBlk, sm.kpl[st],
+                          sm.kpl[st] + KT * 128, 2 * KT * 128, key, c, valid);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.kf[st]);
       // V planes of stage st are free once PV of tile j-2 is done
       if (j >= 2 && !wait_or_abort(&sm.ve[st], ((j >> 1) - 1) & 1, sm, status)) break;
-      pftc::convert_block(sm.raw[rs][1] + lane * REC + c * kBlk, sm.vpl[st][0], sm.vpl[st][1],
-                          lane, c, valid);
+      pftc::convert_block(sm.raw[rs][1] + key * REC + c * kBlk, sm.vpl[st][0], sm.vpl[st][1],
+                          KT * 128, key, c, valid);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -424,10 +448,44 @@ __global__ void __launch_bounds__(pftc::THREADS, 1) prefill_tc_kernel(PrefillArg
 size_t prefill_tc_smem_bytes() { return sizeof(pftc::Smem) + 1024; }
 
 bool prefill_tc_supported(int n_head, int n_kv, int hd, int bf16) {
-  if (!bf16 || hd != 256 || n_kv <= 0 || n_head % n_kv != 0) return false;
+  // the pool's token rows (n_kv * 272 bytes) must be 16-byte multiples for the tensor map
+  if (!bf16 || hd != 256 || n_kv <= 0 || n_head % n_kv != 0 || (n_kv * 272) % 16 != 0)
+    return false;
   const int g = n_head / n_kv;
   return g >= 1 && pftc::ROWS % g == 0;
 }
+
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+// The pool as [n_seq * cap rows][tok_bytes / 4] u32, box = one kv head's record of 32 tokens.
+bool encode_pool_map(CUtensorMap* map, const uint8_t* pool, const PrefillArgs& a) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const uint64_t tok_bytes = (uint64_t)a.n_kv * (a.hd / 32) * kBlk;
+  const cuuint64_t dims[2] = {tok_bytes / 4, (cuuint64_t)a.n_seq * a.cap};
+  const cuuint64_t strides[1] = {tok_bytes};
+  const cuuint32_t box[2] = {pftc::REC / 4, pftc::KT};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(pool), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
 
 cudaError_t launch_prefill_tc(const PrefillArgs& a, cudaStream_t st) {
   static bool attr_set[64] = {};
@@ -440,9 +498,12 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     if (dev < 64) attr_set[dev] = true;
   }
+  CUtensorMap kmap, vmap;
+  if (!encode_pool_map(&kmap, a.k_pool, a) || !encode_pool_map(&vmap, a.v_pool, a))
+    return cudaErrorInvalidValue;
   const int qt = pftc::ROWS / (a.n_head / a.n_kv);
   const dim3 grid(a.n_batch * a.n_kv, (a.n_tok + qt - 1) / qt);
-  prefill_tc_kernel<<<grid, pftc::THREADS, smem, st>>>(a);
+  prefill_tc_kernel<<<grid, pftc::THREADS, smem, st>>>(a, kmap, vmap);
   return cudaGetLastError();
 }
 
