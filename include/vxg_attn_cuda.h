@@ -188,6 +188,12 @@ VXG_ATTN_API int vxg_attn_cuda_q8_decode_partial(void* ctx, void* kv, uint32_t n
 VXG_ATTN_API int vxg_attn_cuda_lse_combine(void* ctx, uint32_t n_parts, uint32_t n_rows, uint32_t head_dim,
                               const float* m, const float* l, const float* o, const float* gate,
                               float* out, int memkind, void* stream, char* err, size_t cap);
+/* The same merge over packed parts, the layout an all-gather of per-rank partials produces:
+ * packed[k] = [m (n_rows) | l (n_rows) | o (n_rows * head_dim)] for k < n_parts. */
+VXG_ATTN_API int vxg_attn_cuda_lse_combine_packed(void* ctx, uint32_t n_parts, uint32_t n_rows,
+                                                  uint32_t head_dim, const float* packed,
+                                                  const float* gate, float* out, int memkind,
+                                                  void* stream, char* err, size_t cap);
 
 /* Drop-in for step_full_gqa_q8 (llm_prefill.rs:259-278) on host buffers for one sequence `seq`
  * of `kv`: q_raw [n_head][hd] (or [n_head][2*hd] with gated_q), k_cur (updated in place with

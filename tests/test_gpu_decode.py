@@ -133,6 +133,11 @@ def test_partials_combine_equal_full(ctx):
     out = vxg_b200.lse_combine(ctx, np.stack(ms), np.stack(ls), np.stack(os_))
     full = pool.decode(seq, np.array([L - 1], np.int32), q)[0]
     np.testing.assert_allclose(out, full, atol=1e-5, rtol=1e-4)
+    # the all-gather layout: per part [m | l | o] packed back to back
+    packed = np.stack([np.concatenate([m_, l_, o_.reshape(-1)]) for m_, l_, o_ in
+                       zip(ms, ls, os_)]).astype(np.float32)
+    out_p = vxg_b200.lse_combine_packed(ctx, packed, len(ms), 16, 256)
+    np.testing.assert_array_equal(out_p, out)
     want = oracle_decode(kh, vh, cap, seq, np.array([L - 1], np.int32), q, 2, 256)[0]
     np.testing.assert_allclose(out, want, atol=ATOL, rtol=RTOL)
 

@@ -6,7 +6,8 @@ importing the operators requires the built library and calling them requires an 
 """
 from ._lib import VxgError, lib  # noqa: F401
 from .attn import (Context, KvQ8Block, KvQ8Pool, deltanet_prefill, deltanet_step,  # noqa: F401
-                   lse_combine, step_deltanet_recurrent, step_full_gqa_q8)
+                   lse_combine, lse_combine_packed, step_deltanet_recurrent, step_full_gqa_q8)
 
 __all__ = ["VxgError", "Context", "KvQ8Block", "KvQ8Pool", "deltanet_prefill", "deltanet_step",
-           "lse_combine", "step_deltanet_recurrent", "step_full_gqa_q8", "lib"]
+           "lse_combine", "lse_combine_packed", "step_deltanet_recurrent", "step_full_gqa_q8",
+           "lib"]

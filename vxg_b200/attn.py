@@ -320,14 +320,17 @@ class KvQ8Pool:
         return out
 
     def decode_partial(self, seq_ids, kv_begin, kv_end, q, scale=None, max_ctx: int = 0,
-                       stream=None):
-        """Per-(b, head) partial (m [log2 units], l, o unnormalised) over [kv_begin, kv_end)."""
+                       stream=None, out=None):
+        """Per-(b, head) partial (m [log2 units], l, o unnormalised) over [kv_begin, kv_end).
+        ``out`` = optional preallocated (m, l, o), e.g. views of one packed send buffer."""
         a = _Args(q)
         B = len(seq_ids) if not a.device else seq_ids.numel()
         n_head = (q.size if not a.device else q.numel()) // (B * self.head_dim)
         if scale is None:
             scale = 1.0 / math.sqrt(self.head_dim)
-        if a.device:
+        if out is not None:
+            m, l, o = out
+        elif a.device:
             import torch
             m = torch.empty((B, n_head), dtype=torch.float32, device=q.device)
             l = torch.empty((B, n_head), dtype=torch.float32, device=q.device)
@@ -363,6 +366,26 @@ def lse_combine(ctx: Context, m, l, o, gate=None, out=None, stream=None):
         a.ptr(o, np.float32, (P, R, hd), "o"), a.ptr(gate, np.float32, (R, hd), "gate"),
         a.ptr(out, np.float32, (R, hd), "out", writable=True), a.memkind, a.stream(stream),
         err.buf, err.cap), err)
+    return out
+
+
+def lse_combine_packed(ctx: Context, packed, n_parts: int, n_rows: int, head_dim: int,
+                       gate=None, out=None, stream=None):
+    """Merge packed partials packed[k] = [m (R) | l (R) | o (R*hd)] -> out [R][hd]."""
+    a = _Args(packed)
+    if out is None:
+        if a.device:
+            import torch
+            out = torch.empty((n_rows, head_dim), dtype=torch.float32, device=packed.device)
+        else:
+            out = np.empty((n_rows, head_dim), np.float32)
+    err = ErrBuf()
+    check(lib().vxg_attn_cuda_lse_combine_packed(
+        ctx.h, n_parts, n_rows, head_dim,
+        a.ptr(packed, np.float32, (n_parts, n_rows * (head_dim + 2)), "packed"),
+        a.ptr(gate, np.float32, (n_rows, head_dim), "gate"),
+        a.ptr(out, np.float32, (n_rows, head_dim), "out", writable=True), a.memkind,
+        a.stream(stream), err.buf, err.cap), err)
     return out
 
 

@@ -742,7 +742,9 @@ int vxg_attn_cuda_q8_decode_partial(void* ctx, void* h, uint32_t n_batch, uint32
     vxg::DecodeArgs a = decode_args(kv, n_batch, n_head, seq_ids, kv_begin, kv_end, 0, q, scale,
                                     max_ctx, c.d_status);
     vxg::Partials p = carve_partials(c, a);
-    check(vxg::launch_decode_partial(a, p, m, l, o, c.sm_count, c.force_generic, st),
+    cudaEvent_t e0, e1;
+    record_timing(c, &e0, &e1);
+    check(vxg::launch_decode_partial(a, p, m, l, o, c.sm_count, c.force_generic, st, e0, e1),
           "decode partial launch");
     sg.download();
     return finish(c, stream, st);
@@ -769,6 +771,30 @@ int vxg_attn_cuda_lse_combine(void* ctx, uint32_t n_parts, uint32_t n_rows, uint
     sg.upload();
     check(vxg::launch_lse_combine((int)n_parts, (int)n_rows, (int)head_dim, m, l, o, gate, out,
                                   c.d_status, st),
+          "lse combine launch");
+    sg.download();
+    return finish(c, stream, st);
+  });
+}
+
+int vxg_attn_cuda_lse_combine_packed(void* ctx, uint32_t n_parts, uint32_t n_rows,
+                                     uint32_t head_dim, const float* packed, const float* gate,
+                                     float* out, int memkind, void* stream, char* err,
+                                     size_t cap) {
+  return guarded(ctx, stream, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    if (n_rows == 0) return VXG_ATTN_OK;
+    require(packed && out, VXG_ATTN_ERR_NULL_PTR, "null input");
+    require(n_parts > 0 && head_dim > 0, VXG_ATTN_ERR_INVALID_OPTION, "empty combine");
+    cudaStream_t st = pick_stream(c, stream);
+    const bool host = memkind == VXG_ATTN_MEM_HOST;
+    Stager sg(c, st, host);
+    sg.in(packed, (size_t)n_parts * n_rows * (head_dim + 2) * sizeof(float));
+    sg.in(gate, (size_t)n_rows * head_dim * sizeof(float));
+    sg.out(out, (size_t)n_rows * head_dim * sizeof(float));
+    sg.upload();
+    check(vxg::launch_lse_combine_packed((int)n_parts, (int)n_rows, (int)head_dim, packed, gate,
+                                         out, c.d_status, st),
           "lse combine launch");
     sg.download();
     return finish(c, stream, st);

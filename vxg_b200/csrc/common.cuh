@@ -32,7 +32,7 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// ---- mbarrier + 1-D bulk async copy (TMA engine, no tensor map, no multicast) ----------------
+// ---- mbarrier + 1-D bulk async copy (TMA engine, no tensor map, local source) ---------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }

@@ -846,22 +846,26 @@ __global__ void __launch_bounds__(256) decode_fast_combine_final(DecodeArgs a, P
   }
 }
 
+// Part k's values of row r: m[k * pstride + r], l[k * pstride + r], o[k * pstride + r*hd + d]
+// (pstride = n_rows for m and l and n_rows*hd for o when they are separate arrays; one common
+// stride n_rows*(hd+2) for the packed [m | l | o] per-part layout of an all-gather).
 __global__ void __launch_bounds__(256) lse_combine_kernel(int n_parts, int n_rows, int hd,
                                                           const float* m, const float* l,
-                                                          const float* o, const float* gate,
+                                                          const float* o, size_t ps_ml,
+                                                          size_t ps_o, const float* gate,
                                                           float* out, uint32_t* status) {
   const int row = blockIdx.x;
   float M = -INFINITY;
-  for (int k = 0; k < n_parts; ++k) M = fmaxf(M, m[(size_t)k * n_rows + row]);
+  for (int k = 0; k < n_parts; ++k) M = fmaxf(M, m[(size_t)k * ps_ml + row]);
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float L = 0.f, O = 0.f;
     if (M != -INFINITY)
       for (int k = 0; k < n_parts; ++k) {
-        const float mk = m[(size_t)k * n_rows + row];
+        const float mk = m[(size_t)k * ps_ml + row];
         if (mk == -INFINITY) continue;
         const float f = exp2f(mk - M);
-        L = fmaf(l[(size_t)k * n_rows + row], f, L);
-        O = fmaf(o[((size_t)k * n_rows + row) * hd + d], f, O);
+        L = fmaf(l[(size_t)k * ps_ml + row], f, L);
+        O = fmaf(o[(size_t)k * ps_o + (size_t)row * hd + d], f, O);
       }
     float r = (L > 0.f || L != L) ? O / L : 0.f;  // NaN partials stay NaN
     const size_t oi = (size_t)row * hd + d;
@@ -1009,10 +1013,12 @@ cudaError_t launch_decode(const DecodeArgs& a, const Partials& part, const float
 
 cudaError_t launch_decode_partial(const DecodeArgs& a, const Partials& part, float* m_out,
                                   float* l_out, float* o_out, int sm_count, int force_generic,
-                                  cudaStream_t st) {
+                                  cudaStream_t st, cudaEvent_t ev0, cudaEvent_t ev1) {
   if (a.n_batch == 0) return cudaSuccess;
   int mode = 0, max_split = 0;
+  if (ev0) cudaEventRecord(ev0, st);
   cudaError_t e = run_split(a, part, sm_count, force_generic, st, &mode, &max_split);
+  if (ev1) cudaEventRecord(ev1, st);
   if (e != cudaSuccess) return e;
   if (mode == 1)
     return launch_fast_combine(a, part, sm_count, nullptr, nullptr, m_out, l_out, o_out, st);
@@ -1026,7 +1032,19 @@ cudaError_t launch_lse_combine(int n_parts, int n_rows, int hd, const float* m, 
                                const float* o, const float* gate, float* out, uint32_t* status,
                                cudaStream_t st) {
   if (n_rows == 0) return cudaSuccess;
-  lse_combine_kernel<<<n_rows, 256, 0, st>>>(n_parts, n_rows, hd, m, l, o, gate, out, status);
+  lse_combine_kernel<<<n_rows, 256, 0, st>>>(n_parts, n_rows, hd, m, l, o, (size_t)n_rows,
+                                             (size_t)n_rows * hd, gate, out, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lse_combine_packed(int n_parts, int n_rows, int hd, const float* packed,
+                                      const float* gate, float* out, uint32_t* status,
+                                      cudaStream_t st) {
+  if (n_rows == 0) return cudaSuccess;
+  const size_t ps = (size_t)n_rows * (hd + 2);
+  lse_combine_kernel<<<n_rows, 256, 0, st>>>(n_parts, n_rows, hd, packed, packed + n_rows,
+                                             packed + 2 * (size_t)n_rows, ps, ps, gate, out,
+                                             status);
   return cudaGetLastError();
 }
 

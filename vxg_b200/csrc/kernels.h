@@ -56,13 +56,18 @@ cudaError_t launch_decode(const DecodeArgs& a, const Partials& part, const float
 // [n_batch][n_head], o_out [n_batch][n_head][hd] (o unnormalised, m in log2 units).
 cudaError_t launch_decode_partial(const DecodeArgs& a, const Partials& part, float* m_out,
                                   float* l_out, float* o_out, int sm_count, int force_generic,
-                                  cudaStream_t stream);
+                                  cudaStream_t stream, cudaEvent_t ev_split_begin,
+                                  cudaEvent_t ev_split_end);
 
 // Log-sum-exp merge of n_parts partial results: m,l [n_parts][n_rows], o [n_parts][n_rows][hd]
 // -> out [n_rows][hd] (normalised, gate optional [n_rows][hd]).
 cudaError_t launch_lse_combine(int n_parts, int n_rows, int hd, const float* m, const float* l,
                                const float* o, const float* gate, float* out, uint32_t* status,
                                cudaStream_t stream);
+// Same merge over packed parts: packed[k] = [m (n_rows) | l (n_rows) | o (n_rows*hd)].
+cudaError_t launch_lse_combine_packed(int n_parts, int n_rows, int hd, const float* packed,
+                                      const float* gate, float* out, uint32_t* status,
+                                      cudaStream_t stream);
 
 // deltanet.cu ------------------------------------------------------------------------------
 struct DeltaNetArgs {

@@ -83,7 +83,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Sm
   }
 }
 
-// 2-D tiled tensor copy global -> shared completing on `bar` (no multicast).
+// 2-D tiled tensor copy global -> shared completing on `bar` (this GPU's memory only).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
   asm volatile(

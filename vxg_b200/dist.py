@@ -72,32 +72,46 @@ class LongContextDecoder:
     """One long sequence split by KV range across the ranks of the default process group.
 
     Owns this rank's slice as a one-sequence KvQ8Pool; ``step`` appends the new token where it
-    belongs and returns the merged attention output (every rank gets it)."""
+    belongs and returns the merged attention output (every rank gets it).  Per step: the split
+    kernels write this rank's (m, l, o) straight into a packed send buffer, one NCCL
+    all_gather_into_tensor exchanges n_head*(head_dim+2) floats per rank, and the packed
+    log-sum-exp combine merges them; all buffers are allocated once."""
 
     def __init__(self, ctx, capacity: int, n_head: int, n_head_kv: int, head_dim: int,
                  world: int, rank: int, group=None):
         from .attn import KvQ8Pool
+        import torch
         self.ctx = ctx
         self.range = KvRange(capacity, world, rank)
         self.pool = KvQ8Pool(ctx, 1, n_head_kv, head_dim, self.range.span)
-        self.n_head, self.head_dim = n_head, head_dim
+        self.n_head, self.head_dim, self.world = n_head, head_dim, world
         self.group = group
-        import torch
-        self._seq = torch.zeros(1, dtype=torch.int32, device="cuda")
-        self._begin = torch.zeros(1, dtype=torch.int32, device="cuda")
-        self._end = torch.zeros(1, dtype=torch.int32, device="cuda")
-        self._pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self._seq = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._begin = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._end = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        per = n_head * (head_dim + 2)
+        self._send = torch.empty(per, dtype=torch.float32, device=dev)
+        self._recv = torch.empty(world * per, dtype=torch.float32, device=dev)
+        self._out = torch.empty((n_head, head_dim), dtype=torch.float32, device=dev)
+        self._m = self._send[:n_head].view(1, n_head)
+        self._l = self._send[n_head:2 * n_head].view(1, n_head)
+        self._o = self._send[2 * n_head:].view(1, n_head, head_dim)
 
     def step(self, pos: int, q, k_new, v_new, scale=None):
         """Append (k_new, v_new) at ``pos`` (on its owner) and attend q over [0, pos]."""
-        from .attn import lse_combine
+        import torch.distributed as dist
+        from .attn import lse_combine_packed
         r = self.range
         if r.owner(pos) == r.rank:
             self._pos.fill_(r.local_pos(pos))
             self.pool.append(self._seq, self._pos, k_new.reshape(1, 1, -1, self.head_dim),
                              v_new.reshape(1, 1, -1, self.head_dim))
         self._end.fill_(r.local_len(pos + 1))
-        m, l, o = self.pool.decode_partial(self._seq, self._begin, self._end,
-                                           q.reshape(1, self.n_head, self.head_dim), scale=scale)
-        M, L, O = all_gather_partials(m, l, o, self.group)
-        return lse_combine(self.ctx, M, L, O)
+        self.pool.decode_partial(self._seq, self._begin, self._end,
+                                 q.reshape(1, self.n_head, self.head_dim), scale=scale,
+                                 out=(self._m, self._l, self._o))
+        dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
+        return lse_combine_packed(self.ctx, self._recv, self.world, self.n_head, self.head_dim,
+                                  out=self._out)
