@@ -110,6 +110,16 @@ VXG_ATTN_API int vxg_attn_cuda_kv_import(void* ctx, void* kv, uint32_t seq, uint
 VXG_ATTN_API int vxg_attn_cuda_kv_export(void* ctx, void* kv, uint32_t seq, uint32_t tok_begin, uint32_t n_tok,
                             void* k_blocks, void* v_blocks, int memkind, char* err, size_t cap);
 
+/* Checkpoint / restore of recurrent state buffers (vxt_metal_cb4_fast_checkpoint,
+ * native/metal_cb4_fast.mm:531-570): for i < n_buffers, copies bytes[i] device bytes from
+ * states[i] to backups[i] (restore == 0) or back (restore != 0), e.g. the DeltaNet ssm and conv
+ * states of every recurrent layer before a speculative step.  Device-to-device, on `stream`
+ * (asynchronous) or synchronous when stream is NULL. */
+VXG_ATTN_API int vxg_attn_cuda_state_checkpoint(void* ctx, uint32_t n_buffers, void* const* states,
+                                                void* const* backups, const size_t* bytes,
+                                                uint32_t restore, void* stream, char* err,
+                                                size_t cap);
+
 /* ---------------------------------------------------------------- ops ---------------------- */
 /* Quantise-and-append (llm_prefill.rs:311-324 with KvQ8Block::quantize, :27-42), bit-exact:
  * for b < n_batch, t < n_tok: k_new/v_new[b][t][n_head_kv][head_dim] (f32, mem) go to sequence

@@ -61,6 +61,32 @@ def test_deltanet_device_resident_state(ctx):
     np.testing.assert_array_equal(dstate.cpu().numpy(), state)
 
 
+def test_state_checkpoint_restore_rolls_back_a_step(ctx):
+    """vxg_attn_cuda_state_checkpoint (native/metal_cb4_fast.mm:531-570): save the ssm and conv
+    states, run a step, restore; the states are bit-identical to the saved ones and a replayed
+    step reproduces the first output exactly."""
+    import torch
+    rng = np.random.default_rng(33)
+    B, H, dk, dv = 2, 4, 128, 128
+    state = torch.from_numpy((rng.standard_normal((B, H, dv, dk)) * 0.02).astype(np.float32)).cuda()
+    conv = torch.from_numpy(rng.standard_normal((B, 3, 1024)).astype(np.float32)).cuda()
+    saved = [state.clone(), conv.clone()]
+    bak = [torch.empty_like(state), torch.empty_like(conv)]
+    A = -torch.ones(H, device="cuda")
+    dt = torch.zeros(H, device="cuda")
+    q, k, v, br, ar = [torch.from_numpy(x).cuda() for x in inputs(rng, B, H, H, dk, dv)]
+    assert ctx.checkpoint([state, conv], bak) == 0
+    o1 = vxg_b200.deltanet_step(ctx, q, k, v, br, ar, A, dt, state).clone()
+    conv.add_(1.0)
+    assert not torch.equal(state, saved[0])
+    assert ctx.checkpoint([state, conv], bak, restore=True) == 0
+    ctx.sync()
+    assert torch.equal(state, saved[0]) and torch.equal(conv, saved[1])
+    o2 = vxg_b200.deltanet_step(ctx, q, k, v, br, ar, A, dt, state)
+    ctx.sync()
+    assert torch.equal(o1, o2)
+
+
 def test_deltanet_rejects_bad_shapes(ctx):
     rng = np.random.default_rng(32)
     state = np.zeros((1, 4, 32, 96), np.float32)

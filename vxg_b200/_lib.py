@@ -63,6 +63,7 @@ SIGNATURES = {
     "vxg_attn_cuda_q8_decode_partial": (_I, [_P, _P, _U, _U, _P, _P, _P, _P, _F, _U, _P, _P, _P,
                                              _I, _P, _C, _S]),
     "vxg_attn_cuda_lse_combine": (_I, [_P, _U, _U, _U, _P, _P, _P, _P, _P, _I, _P, _C, _S]),
+    "vxg_attn_cuda_state_checkpoint": (_I, [_P, _U, _P, _P, _P, _U, _P, _C, _S]),
     "vxg_attn_cuda_lse_combine_packed": (_I, [_P, _U, _U, _U, _P, _P, _P, _I, _P, _C, _S]),
     "vxg_attn_cuda_step_full_gqa_q8": (_I, [_P, _P, _U, _P, _P, _P, _P, _P, _I, _U, _U, _U, _U,
                                             _U, _U, _F, _I, _F, _P, _C, _S]),

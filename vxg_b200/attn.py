@@ -149,6 +149,26 @@ class Context:
     def force_generic(self, enable: bool):
         lib().vxg_attn_cuda_force_generic(self.h, int(enable))
 
+    def checkpoint(self, states, backups, restore: bool = False, stream=None):
+        """Copy each device tensor of ``states`` into the matching one of ``backups`` (or back
+        with restore=True): vxg_attn_cuda_state_checkpoint, asynchronous on the stream."""
+        import torch
+        n = len(states)
+        if len(backups) != n:
+            raise ValueError("states and backups differ in length")
+        for s_, b_ in zip(states, backups):
+            if s_.numel() * s_.element_size() != b_.numel() * b_.element_size():
+                raise ValueError("state and backup sizes differ")
+        src = (ctypes.c_void_p * n)(*[s_.data_ptr() for s_ in states])
+        dst = (ctypes.c_void_p * n)(*[b_.data_ptr() for b_ in backups])
+        nb = (ctypes.c_size_t * n)(*[s_.numel() * s_.element_size() for s_ in states])
+        s = stream if stream is not None else torch.cuda.current_stream()
+        err = ErrBuf()
+        return check(lib().vxg_attn_cuda_state_checkpoint(
+            self.h, n, ctypes.cast(src, ctypes.c_void_p), ctypes.cast(dst, ctypes.c_void_p),
+            ctypes.cast(nb, ctypes.c_void_p), int(restore), _stream_handle(s), err.buf, err.cap),
+            err)
+
     def host_alloc(self, nbytes: int):
         err = ErrBuf()
         p = lib().vxg_attn_cuda_host_alloc(self.h, nbytes, err.buf, err.cap)

@@ -566,6 +566,25 @@ int vxg_attn_cuda_kv_export(void* ctx, void* kv, uint32_t seq, uint32_t tok_begi
 }
 
 // ---------------------------------------------------------------- ops --------------------------
+int vxg_attn_cuda_state_checkpoint(void* ctx, uint32_t n_buffers, void* const* states,
+                                   void* const* backups, const size_t* bytes, uint32_t restore,
+                                   void* stream, char* err, size_t cap) {
+  return guarded(ctx, stream, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    if (n_buffers == 0) return VXG_ATTN_OK;
+    require(states && backups && bytes, VXG_ATTN_ERR_NULL_PTR, "null buffer list");
+    cudaStream_t st = pick_stream(c, stream);
+    for (uint32_t i = 0; i < n_buffers; ++i) {
+      if (bytes[i] == 0) continue;
+      require(states[i] && backups[i], VXG_ATTN_ERR_NULL_PTR, "null state or backup buffer");
+      check(cudaMemcpyAsync(restore ? states[i] : backups[i], restore ? backups[i] : states[i],
+                            bytes[i], cudaMemcpyDeviceToDevice, st),
+            "checkpoint copy");
+    }
+    return finish(c, stream, st);
+  });
+}
+
 int vxg_attn_cuda_q8_append(void* ctx, void* h, uint32_t n_batch, uint32_t n_tok,
                             const int32_t* seq_ids, const int32_t* pos, const float* k_new,
                             const float* v_new, int memkind, void* stream, char* err, size_t cap) {
