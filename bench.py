@@ -505,7 +505,7 @@ def run_dnet_prefill(args, world, rank, local):
     """BASELINE config 5b: gated-DeltaNet prefill of 8 prompts x 8192 tokens per GPU, 32 heads,
     dk = dv = 128, the decode config's distributions (q, k, v N(0,1), beta = sigmoid(N(0,1)),
     decay exp(-softplus(N(0,1)))).  One step = vxg_attn_cuda_deltanet_prefill over all prompts
-    (state held on chip across the prompt)."""
+    (chunked WY form, 64-token chunks, state rows held on chip)."""
     import torch
     import torch.distributed as dist
     import vxg_b200
@@ -552,12 +552,12 @@ def run_dnet_prefill(args, world, rank, local):
         "config": {"workload": f"config5b: DeltaNet prefill, {B} prompts x 8192 tokens per GPU, "
                                "32 heads, dk=dv=128, state N(0,0.02^2) on chip",
                    "l2": "inputs larger than L2 (4.3 GB of q/k/v/o per step)"},
-        "roofline": {"kernel": "deltanet_prefill_kernel", "bound": "tensor", "achieved": ach,
+        "roofline": {"kernel": "deltanet_chunk_kernel", "bound": "tensor", "achieved": ach,
                      "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                      "peak_kind": peak_kind + " (sustained bf16)",
                      "flop_per_launch": 2 * mac,
-                     "note": "FLOPs of the chunked (WY, C=64) algorithm; the kernel runs the "
-                             "sequential recurrence"},
+                     "note": "FLOPs of the chunked (WY, C=64) algorithm, which the kernel "
+                             "runs on mma.sync TF32 (3xTF32 for the solve and state update)"},
         "gpu_launches": 3 * K, "clocks": sampler.summary(),
     }
     ctx.close()

@@ -127,6 +127,36 @@ def test_deltanet_prefill_matches_token_by_token_oracle(ctx, B, T, n_kh, n_vh, d
     np.testing.assert_allclose(state, ref, atol=ATOL, rtol=RTOL)
 
 
+@pytest.mark.parametrize("B,T,n_kh,n_vh,dv,generic", [
+    (2, 300, 2, 4, 64, False),      # chunked (WY) tensor-core path: 5 chunks, the last partial
+    (1, 4096, 2, 2, 128, False),    # config-5b prompt length, 64 chunks
+    (2, 300, 2, 4, 64, True),       # the sequential kernel on the same shapes
+])
+def test_deltanet_prefill_chunked_matches_sequential_oracle(ctx, B, T, n_kh, n_vh, dv, generic):
+    """dk = 128 prompts run the chunked (WY) form; it must match the token-by-token fp32
+    recurrence of the reference (llm_prefill.rs:470-480) within the bar, outputs and state."""
+    rng = np.random.default_rng(34 + T)
+    dk = 128
+    state = (rng.standard_normal((B, n_vh, dv, dk)) * 0.02).astype(np.float32)
+    ref = state.copy()
+    A = -np.exp(rng.standard_normal(n_vh) * 0.3).astype(np.float32)
+    dt = (rng.standard_normal(n_vh) * 0.1).astype(np.float32)
+    q, k, v, br, ar = seq_inputs(rng, B, T, n_kh, n_vh, dk, dv)
+    ctx.force_generic(generic)
+    try:
+        o = vxg_b200.deltanet_prefill(ctx, q, k, v, br, ar, A, dt, state)
+    finally:
+        ctx.force_generic(False)
+    worst = 0.0
+    for t in range(T):
+        ro = oracle.batch_deltanet(q[:, t], k[:, t], v[:, t], br[:, t], ar[:, t], A, dt, n_kh,
+                                   n_vh, dk, dv, 1e-6, 1 / np.sqrt(dk), ref, n_threads=8)
+        np.testing.assert_allclose(o[:, t], ro, atol=ATOL, rtol=RTOL, err_msg=f"token {t}")
+        worst = max(worst, float((np.abs(o[:, t] - ro) / (ATOL + RTOL * np.abs(ro))).max()))
+    np.testing.assert_allclose(state, ref, atol=ATOL, rtol=RTOL)
+    assert worst < 0.25, worst
+
+
 def test_deltanet_prefill_equals_decode_steps_long(ctx):
     """Config-5b-like length: the on-chip recurrence over 2048 tokens equals 2048 decode steps
     (both on the GPU; size-independent property)."""

@@ -1018,7 +1018,8 @@ int vxg_attn_cuda_deltanet_prefill(void* ctx, uint32_t n_batch, uint32_t n_tok, 
     a.q_scale = q_scale;
     a.status = c.d_status;
     c.aux2.reserve(vxg::deltanet_prefill_scratch_bytes(a), "cudaMalloc deltanet scratch");
-    check(vxg::launch_deltanet_prefill(a, c.aux2.p, st), "deltanet prefill launch");
+    check(vxg::launch_deltanet_prefill(a, c.aux2.p, !c.force_generic, st),
+          "deltanet prefill launch");
     sg.download();
     return finish(c, stream, st);
   });

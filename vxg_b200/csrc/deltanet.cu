@@ -25,10 +25,13 @@ namespace {
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x / (1.0f + expf(-x)); }
 // llm_ops.rs:156-165
-__device__ __forceinline__ float decay_of(float alpha_raw, float dt_bias, float A) {
+__device__ __forceinline__ float log_decay_of(float alpha_raw, float dt_bias, float A) {
   const float x = alpha_raw + dt_bias;
   const float sp = x > 20.0f ? x : (x < -20.0f ? expf(x) : logf(1.0f + expf(x)));
-  return expf(sp * A);
+  return sp * A;
+}
+__device__ __forceinline__ float decay_of(float alpha_raw, float dt_bias, float A) {
+  return expf(log_decay_of(alpha_raw, dt_bias, A));
 }
 }  // namespace
 
@@ -300,7 +303,7 @@ __global__ void __launch_bounds__(256, 1) deltanet_step_persistent(DeltaNetArgs 
 // Preparation pass: normalised q, k per (b, t, k head) and (beta, decay) per (b, t, v head).
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) deltanet_prep_kernel(DeltaNetArgs a, float* qn, float* kn,
-                                                            float2* gates) {
+                                                            float2* gates, float* lgs) {
   // blockIdx.x = (b * n_tok + t) ; threads cover the k heads (warp per head) then the gates
   const int bt = blockIdx.x;
   const int b = bt / a.n_tok, t = bt - b * a.n_tok;
@@ -325,8 +328,9 @@ __global__ void __launch_bounds__(128) deltanet_prep_kernel(DeltaNetArgs a, floa
   }
   for (int h = threadIdx.x; h < a.n_vh; h += blockDim.x) {
     const size_t gi = (size_t)b * a.g_bs + (size_t)t * a.g_ts + h;
-    gates[(size_t)bt * a.n_vh + h] =
-        make_float2(sigmoidf_(a.beta_raw[gi]), decay_of(a.alpha_raw[gi], a.dt_bias[h], a.ssm_a[h]));
+    const float lg = log_decay_of(a.alpha_raw[gi], a.dt_bias[h], a.ssm_a[h]);
+    gates[(size_t)bt * a.n_vh + h] = make_float2(sigmoidf_(a.beta_raw[gi]), expf(lg));
+    if (lgs) lgs[(size_t)bt * a.n_vh + h] = lg;
   }
 }
 
@@ -478,26 +482,34 @@ cudaError_t launch_deltanet_step(const DeltaNetArgs& a, cudaStream_t st) {
 
 size_t deltanet_prefill_scratch_bytes(const DeltaNetArgs& a) {
   const size_t bt = (size_t)a.n_batch * a.n_tok;
-  return (2 * bt * a.n_kh * a.dk) * sizeof(float) + bt * a.n_vh * sizeof(float2) + 256;
+  return (2 * bt * a.n_kh * a.dk) * sizeof(float) + bt * a.n_vh * (sizeof(float2) + sizeof(float)) +
+         256;
 }
 
-cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, cudaStream_t st) {
+cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, int allow_chunk,
+                                    cudaStream_t st) {
   if (a.n_batch == 0 || a.n_tok == 0 || a.n_vh == 0) return cudaSuccess;
   const size_t bt = (size_t)a.n_batch * a.n_tok;
   float* qn = static_cast<float*>(scratch);
   float* kn = qn + bt * a.n_kh * a.dk;
   float2* gates = reinterpret_cast<float2*>(kn + bt * a.n_kh * a.dk);
-  deltanet_prep_kernel<<<(unsigned)bt, 128, 0, st>>>(a, qn, kn, gates);
+  float* lgs = reinterpret_cast<float*>(gates + bt * a.n_vh);
+  const bool chunked = allow_chunk && deltanet_chunk_supported(a);
+  deltanet_prep_kernel<<<(unsigned)bt, 128, 0, st>>>(a, qn, kn, gates, chunked ? lgs : nullptr);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const unsigned grid = (unsigned)(a.n_batch * a.n_vh * (a.dv / 32));
-  switch (a.dk) {
-    case 64: deltanet_prefill_kernel<64><<<grid, 256, 0, st>>>(a, qn, kn, gates); break;
-    case 128: deltanet_prefill_kernel<128><<<grid, 256, 0, st>>>(a, qn, kn, gates); break;
-    case 256: deltanet_prefill_kernel<256><<<grid, 256, 0, st>>>(a, qn, kn, gates); break;
-    default: return cudaErrorInvalidValue;
+  if (chunked) {
+    e = launch_deltanet_chunk(a, qn, kn, gates, lgs, st);
+  } else {
+    const unsigned grid = (unsigned)(a.n_batch * a.n_vh * (a.dv / 32));
+    switch (a.dk) {
+      case 64: deltanet_prefill_kernel<64><<<grid, 256, 0, st>>>(a, qn, kn, gates); break;
+      case 128: deltanet_prefill_kernel<128><<<grid, 256, 0, st>>>(a, qn, kn, gates); break;
+      case 256: deltanet_prefill_kernel<256><<<grid, 256, 0, st>>>(a, qn, kn, gates); break;
+      default: return cudaErrorInvalidValue;
+    }
+    e = cudaGetLastError();
   }
-  e = cudaGetLastError();
   if (e != cudaSuccess || !a.y) return e;
   const int rows = a.n_batch * a.n_tok * a.n_vh;
   deltanet_epilogue_kernel<<<(rows + 7) / 8, 256, 0, st>>>(a);

@@ -94,8 +94,17 @@ struct DeltaNetArgs {
 cudaError_t launch_deltanet_step(const DeltaNetArgs& a, cudaStream_t stream);
 // n_tok tokens per sequence with the state held on chip; needs deltanet_prefill_scratch_bytes of
 // device scratch.  Writes o (and y with the epilogue when y != nullptr).
+// allow_chunk: dk 128 and dv a multiple of 64 with at least 64 tokens run the chunked (WY)
+// tensor-core kernel (deltanet_chunk.cu); otherwise the sequential on-chip recurrence.
 size_t deltanet_prefill_scratch_bytes(const DeltaNetArgs& a);
-cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, cudaStream_t stream);
+cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, int allow_chunk,
+                                    cudaStream_t stream);
+// deltanet_chunk.cu: qn / kn normalised q, k [b][t][n_kh][128], gates (beta, decay) and lgs
+// (log decay) [b][t][n_vh] from the prep kernel.
+bool deltanet_chunk_supported(const DeltaNetArgs& a);
+size_t deltanet_chunk_smem_bytes();
+cudaError_t launch_deltanet_chunk(const DeltaNetArgs& a, const float* qn, const float* kn,
+                                  const float2* gates, const float* lgs, cudaStream_t stream);
 // conv1d + SiLU over the rolling history (llm_ops.rs:122-137), batched.
 cudaError_t launch_deltanet_conv(const float* x, const float* w, float* conv_state, float* out,
                                  int n_batch, int conv_ch, int k_sz, cudaStream_t stream);
