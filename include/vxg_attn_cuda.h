@@ -120,6 +120,16 @@ VXG_ATTN_API int vxg_attn_cuda_state_checkpoint(void* ctx, uint32_t n_buffers, v
                                                 uint32_t restore, void* stream, char* err,
                                                 size_t cap);
 
+/* fp32 KV pools (KvCacheMode::Fp32, the reference's default, llm.rs:287): the per-layer
+ * `k_caches` / `v_caches` vectors of LlmState (llm.rs:36-41) as device pools of
+ * float[n_seq][cap_tokens][n_head_kv][head_dim] (token rows appended as in llm_ops.rs:256-257).
+ * head_dim must be a multiple of 32 and at most 256.  kv_bytes, kv_capacity, kv_reserve,
+ * kv_device_ptrs, kv_import and kv_export work on these pools too (import / export move raw
+ * f32 rows: n_tok * n_head_kv * head_dim floats per cache). */
+VXG_ATTN_API void* vxg_attn_cuda_kv_create_f32(void* ctx, uint32_t n_seq, uint32_t n_head_kv,
+                                               uint32_t head_dim, uint32_t cap_tokens, char* err,
+                                               size_t cap);
+
 /* ---------------------------------------------------------------- ops ---------------------- */
 /* Quantise-and-append (llm_prefill.rs:311-324 with KvQ8Block::quantize, :27-42), bit-exact:
  * for b < n_batch, t < n_tok: k_new/v_new[b][t][n_head_kv][head_dim] (f32, mem) go to sequence
@@ -159,6 +169,21 @@ VXG_ATTN_API int vxg_attn_cuda_q8_decode_noalloc(
     uint32_t head_dim, uint32_t n_batch, uint32_t n_head, const int32_t* seq_ids,
     const int32_t* pos, const float* q, const float* k_new, const float* v_new,
     const float* q_gate, float scale, float* out, void* stream, char* err, size_t cap);
+
+/* fp32-KV counterparts of vxg_attn_cuda_q8_append / _q8_decode on pools from
+ * vxg_attn_cuda_kv_create_f32: the append copies k_new/v_new rows (llm_ops.rs:256-257) and the
+ * attention is step_full_gqa's (llm_ops.rs:258-299): scores q.k * scale, softmax, sum p v,
+ * optional sigmoid gate.  Same arguments and layouts as the Q8 calls. */
+VXG_ATTN_API int vxg_attn_cuda_f32_append(void* ctx, void* kv, uint32_t n_batch, uint32_t n_tok,
+                                          const int32_t* seq_ids, const int32_t* pos,
+                                          const float* k_new, const float* v_new, int memkind,
+                                          void* stream, char* err, size_t cap);
+VXG_ATTN_API int vxg_attn_cuda_f32_decode(void* ctx, void* kv, uint32_t n_batch, uint32_t n_head,
+                                          const int32_t* seq_ids, const int32_t* pos,
+                                          const float* q, const float* k_new, const float* v_new,
+                                          const float* q_gate, float scale, uint32_t max_ctx,
+                                          float* out, int memkind, void* stream, char* err,
+                                          size_t cap);
 
 /* Chunked prefill of n_tok prompt tokens per sequence, the batched form of what the reference
  * runs token by token (prefill_cpu_tiled, llm_prefill.rs:497-527, calling step_full_gqa_q8,
@@ -216,6 +241,18 @@ VXG_ATTN_API int vxg_attn_cuda_step_full_gqa_q8(void* ctx, void* kv, uint32_t se
                                    uint32_t rope_pos, uint32_t rope_dim, float rope_freq_base,
                                    int rope_neox, float eps, float* attn_out, char* err,
                                    size_t cap);
+
+/* Drop-in for step_full_gqa (crates/vxg-tensor/src/llm_ops.rs:196-300), the fp32-KV operator:
+ * the same argument list (q_raw, k_cur updated in place, v_cur, norms, gated_q, shapes, pos,
+ * RoPE at pos, eps, att_cat out) with the layer's fp32 pool + sequence id in place of
+ * `&mut Vec<f32>` caches.  Host buffers; synchronous. */
+VXG_ATTN_API int vxg_attn_cuda_step_full_gqa(void* ctx, void* kv, uint32_t seq, const float* q_raw,
+                                             float* k_cur, const float* v_cur,
+                                             const float* q_norm, const float* k_norm,
+                                             int gated_q, uint32_t n_head, uint32_t n_head_kv,
+                                             uint32_t head_dim, uint32_t pos, uint32_t rope_dim,
+                                             float rope_freq_base, int rope_neox, float eps,
+                                             float* att_cat, char* err, size_t cap);
 
 /* Gated-DeltaNet core step (llm_ops.rs:139-184) for n_batch sequences:
  * q, k [n_batch][n_kh][dk] (raw, L2-normalised inside, q also scaled by q_scale, 1/sqrt(dk) in

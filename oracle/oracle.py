@@ -51,6 +51,9 @@ def lib():
             L.vxo_q8_dot.argtypes = [_p, _p]
             L.vxo_q8_append.argtypes = [_p, _p, _sz, _sz, _sz, _p, _p]
             L.vxo_q8_attend.argtypes = [_p, _p, _p, _p, _sz, _sz, _sz, _sz, _f, _p, _p]
+            L.vxo_f32_attend.argtypes = [_p, _p, _p, _p, _sz, _sz, _sz, _sz, _f, _p, _p]
+            L.vxo_step_full_gqa.argtypes = [_p, _p, _p, _p, _p, ctypes.c_int, _sz, _sz, _sz, _sz,
+                                            _sz, _f, ctypes.c_int, _f, _p, _p, _p]
             L.vxo_step_full_gqa_q8.argtypes = [
                 _p, _p, _p, _p, _p, ctypes.c_int, _sz, _sz, _sz, _sz, _sz, _sz, _f,
                 ctypes.c_int, _f, _p, _p, _p]
@@ -156,6 +159,32 @@ def batch_decode_q8(seq_ids, pos, q, k_new, v_new, k_pool, v_pool, cap, n_head, 
     lib().vxo_batch_decode_q8(B, _ptr(seq_ids), _ptr(pos), _ptr(q), _ptr(kn), _ptr(vn), _ptr(g),
                               _ptr(k_pool), _ptr(v_pool), cap, n_head, n_kv, hd, _f(scale),
                               int(bool(do_append)), _ptr(out), int(n_threads))
+    return out
+
+
+def f32_attend(q_heads, k_cache, v_cache, n_head, n_kv, hd, seq_len, scale=None, gates=None):
+    """llm_ops.rs:255-299: attention over fp32 caches [t][n_kv][hd] for tokens [0, seq_len)."""
+    q_heads = _f32(q_heads)
+    out = np.zeros(n_head * hd, dtype=np.float32)
+    if scale is None:
+        scale = 1.0 / np.sqrt(np.float32(hd))
+    g = _f32(gates) if gates is not None else None
+    lib().vxo_f32_attend(_ptr(q_heads), _ptr(g), _ptr(_f32(k_cache)), _ptr(_f32(v_cache)), n_head,
+                         n_kv, hd, seq_len, _f(scale), _ptr(out), None)
+    return out.reshape(n_head, hd)
+
+
+def step_full_gqa(q_raw, k_cur, v_cur, q_norm, k_norm, gated_q, n_head, n_head_kv, head_dim, pos,
+                  rope_dim, rope_freq_base, rope_neox, eps, k_cache, v_cache):
+    """Whole llm_ops.rs:196-300.  k_cur is updated in place; k_cache / v_cache are f32 arrays of
+    at least (pos+1) rows of [n_kv][hd], row pos written.  Returns att_cat [n_head*hd]."""
+    out = np.zeros(n_head * head_dim, dtype=np.float32)
+    qn = _f32(q_norm) if q_norm is not None else None
+    kn = _f32(k_norm) if k_norm is not None else None
+    lib().vxo_step_full_gqa(_ptr(_f32(q_raw)), _ptr(k_cur), _ptr(_f32(v_cur)), _ptr(qn), _ptr(kn),
+                            int(bool(gated_q)), n_head, n_head_kv, head_dim, pos, rope_dim,
+                            _f(rope_freq_base), int(bool(rope_neox)), _f(eps), _ptr(k_cache),
+                            _ptr(v_cache), _ptr(out))
     return out
 
 

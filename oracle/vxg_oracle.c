@@ -295,6 +295,93 @@ void vxo_step_full_gqa_q8(const float* q_raw, float* k_cur, const float* v_cur, 
     free(q_heads);
 }
 
+/* ---- step_full_gqa attention over fp32 caches, llm_ops.rs:255-299 ------------------------ *
+ * k_cache / v_cache: [t][n_kv][hd] f32 holding at least seq_len tokens. */
+void vxo_f32_attend(const float* q_heads, const float* gates, const float* k_cache,
+                    const float* v_cache, size_t n_head, size_t n_kv, size_t hd, size_t seq_len,
+                    float scale, float* att_cat, float* scores) {
+    size_t kv_stride = n_kv * hd;
+    size_t gqa_mul = n_head / n_kv;
+    int own = 0;
+    if (!scores) {
+        scores = (float*)malloc(sizeof(float) * (seq_len ? seq_len : 1));
+        own = 1;
+    }
+    for (size_t h = 0; h < n_head; ++h) {
+        size_t kv_h = h / gqa_mul;
+        const float* qh = q_heads + h * hd;
+        float max_s = -INFINITY;
+        for (size_t t = 0; t < seq_len; ++t) {
+            const float* kh = k_cache + t * kv_stride + kv_h * hd;
+            float dot = 0.0f;
+            for (size_t d = 0; d < hd; ++d) dot = fmaf(qh[d], kh[d], dot);
+            float s = dot * scale;
+            scores[t] = s;
+            if (s > max_s) max_s = s;
+        }
+        float sum_exp = 0.0f;
+        for (size_t t = 0; t < seq_len; ++t) {
+            scores[t] = expf(scores[t] - max_s);
+            sum_exp += scores[t];
+        }
+        float inv_sum = 1.0f / sum_exp;
+        float* out_h = att_cat + h * hd;
+        for (size_t d = 0; d < hd; ++d) out_h[d] = 0.0f;
+        for (size_t t = 0; t < seq_len; ++t) {
+            float w = scores[t] * inv_sum;
+            const float* vh = v_cache + t * kv_stride + kv_h * hd;
+            for (size_t d = 0; d < hd; ++d) out_h[d] = fmaf(w, vh[d], out_h[d]);
+        }
+        if (gates) {
+            const float* gh = gates + h * hd;
+            for (size_t d = 0; d < hd; ++d) out_h[d] *= 1.0f / (1.0f + expf(-gh[d]));
+        }
+    }
+    if (own) free(scores);
+}
+
+/* ---- step_full_gqa, llm_ops.rs:196-300 (whole function): the fp32-KV operator ----------- *
+ * k_cache / v_cache: [>= pos+1][n_kv][hd]; the token is written at row pos (the reference
+ * extends its vectors, so row pos is the new last row). */
+void vxo_step_full_gqa(const float* q_raw, float* k_cur, const float* v_cur, const float* q_norm,
+                       const float* k_norm, int gated_q, size_t n_head, size_t n_kv, size_t hd,
+                       size_t pos, size_t rope_dim, float rope_freq_base, int rope_neox, float eps,
+                       float* k_cache, float* v_cache, float* att_cat) {
+    float* q_cur = (float*)malloc(sizeof(float) * n_head * hd);
+    float* q_gate = gated_q ? (float*)malloc(sizeof(float) * n_head * hd) : NULL;
+    float* tmp = (float*)malloc(sizeof(float) * hd);
+    for (size_t h = 0; h < n_head; ++h) {
+        if (gated_q) {
+            memcpy(q_cur + h * hd, q_raw + h * 2 * hd, sizeof(float) * hd);
+            memcpy(q_gate + h * hd, q_raw + h * 2 * hd + hd, sizeof(float) * hd);
+        } else {
+            memcpy(q_cur + h * hd, q_raw + h * hd, sizeof(float) * hd);
+        }
+    }
+    if (q_norm)
+        for (size_t h = 0; h < n_head; ++h) {
+            memcpy(tmp, q_cur + h * hd, sizeof(float) * hd);
+            vxo_rms_norm(tmp, q_norm, eps, q_cur + h * hd, hd);
+        }
+    if (k_norm)
+        for (size_t h = 0; h < n_kv; ++h) {
+            memcpy(tmp, k_cur + h * hd, sizeof(float) * hd);
+            vxo_rms_norm(tmp, k_norm, eps, k_cur + h * hd, hd);
+        }
+    for (size_t h = 0; h < n_head; ++h)
+        vxo_apply_rope(q_cur + h * hd, hd, pos, rope_dim, rope_freq_base, rope_neox);
+    for (size_t h = 0; h < n_kv; ++h)
+        vxo_apply_rope(k_cur + h * hd, hd, pos, rope_dim, rope_freq_base, rope_neox);
+    memcpy(k_cache + pos * n_kv * hd, k_cur, sizeof(float) * n_kv * hd);
+    memcpy(v_cache + pos * n_kv * hd, v_cur, sizeof(float) * n_kv * hd);
+    float scale = 1.0f / sqrtf((float)hd);
+    vxo_f32_attend(q_cur, q_gate, k_cache, v_cache, n_head, n_kv, hd, pos + 1, scale, att_cat,
+                   NULL);
+    free(tmp);
+    free(q_gate);
+    free(q_cur);
+}
+
 /* ---- gated-DeltaNet core, llm_ops.rs:139-184 ----------------------------------------------- *
  * q_all/k_all: [n_kh][dk] (before L2 norm); v_all: [n_vh][dv]; state: [n_vh][dv][dk] updated in
  * place; o: [n_vh][dv] = S_new q (before the RMSNorm / SiLU(z) epilogue).  q_scale is

@@ -58,6 +58,12 @@ SIGNATURES = {
                                      _C, _S]),
     "vxg_attn_cuda_q8_decode_noalloc": (_I, [_P, _P, _U, _U, _U, _U, _U, _U, _P, _P, _P, _P, _P,
                                              _P, _F, _P, _P, _C, _S]),
+    "vxg_attn_cuda_kv_create_f32": (_P, [_P, _U, _U, _U, _U, _C, _S]),
+    "vxg_attn_cuda_f32_append": (_I, [_P, _P, _U, _U, _P, _P, _P, _P, _I, _P, _C, _S]),
+    "vxg_attn_cuda_f32_decode": (_I, [_P, _P, _U, _U, _P, _P, _P, _P, _P, _P, _F, _U, _P, _I, _P,
+                                      _C, _S]),
+    "vxg_attn_cuda_step_full_gqa": (_I, [_P, _P, _U, _P, _P, _P, _P, _P, _I, _U, _U, _U, _U, _U,
+                                         _F, _I, _F, _P, _C, _S]),
     "vxg_attn_cuda_q8_prefill": (_I, [_P, _P, _U, _U, _U, _P, _P, _P, _P, _P, _P, _I, _F, _U, _P,
                                       _I, _P, _C, _S]),
     "vxg_attn_cuda_q8_decode_partial": (_I, [_P, _P, _U, _U, _P, _P, _P, _P, _F, _U, _P, _P, _P,

@@ -370,6 +370,108 @@ class KvQ8Pool:
         return m, l, o
 
 
+class KvF32Pool:
+    """Device fp32 K/V pools float[n_seq][cap][n_head_kv][head_dim] (KvCacheMode::Fp32, the
+    reference's default cache mode; vxg_attn_cuda_kv_create_f32)."""
+
+    def __init__(self, ctx: Context, n_seq: int, n_head_kv: int, head_dim: int, cap_tokens: int):
+        self.ctx = ctx
+        err = ErrBuf()
+        self.h = lib().vxg_attn_cuda_kv_create_f32(ctx.h, n_seq, n_head_kv, head_dim, cap_tokens,
+                                                   err.buf, err.cap)
+        if not self.h:
+            raise VxgError(-2, "vxg_attn_cuda_kv_create_f32 failed: " + err.text)
+        self.n_seq, self.n_head_kv, self.head_dim = n_seq, n_head_kv, head_dim
+        self.last_rc = 0
+
+    close = KvQ8Pool.close
+    __del__ = KvQ8Pool.__del__
+    capacity = KvQ8Pool.capacity
+    nbytes = KvQ8Pool.nbytes
+    reserve = KvQ8Pool.reserve
+    device_ptrs = KvQ8Pool.device_ptrs
+
+    def import_rows(self, seq: int, tok_begin: int, k_rows, v_rows):
+        """k/v_rows: float32 (n_tok, n_head_kv, head_dim), host."""
+        k_rows = np.ascontiguousarray(k_rows, np.float32)
+        v_rows = np.ascontiguousarray(v_rows, np.float32)
+        n_tok = k_rows.size // (self.n_head_kv * self.head_dim)
+        err = ErrBuf()
+        check(lib().vxg_attn_cuda_kv_import(self.ctx.h, self.h, seq, tok_begin, n_tok,
+                                            k_rows.ctypes.data_as(ctypes.c_void_p),
+                                            v_rows.ctypes.data_as(ctypes.c_void_p), MEM_HOST,
+                                            err.buf, err.cap), err)
+
+    def export_rows(self, seq: int, tok_begin: int, n_tok: int):
+        shape = (n_tok, self.n_head_kv, self.head_dim)
+        k = np.empty(shape, np.float32)
+        v = np.empty(shape, np.float32)
+        err = ErrBuf()
+        check(lib().vxg_attn_cuda_kv_export(self.ctx.h, self.h, seq, tok_begin, n_tok,
+                                            k.ctypes.data_as(ctypes.c_void_p),
+                                            v.ctypes.data_as(ctypes.c_void_p), MEM_HOST,
+                                            err.buf, err.cap), err)
+        return k, v
+
+    def append(self, seq_ids, pos, k_new, v_new, n_tok: int = 1, stream=None) -> int:
+        a = _Args(k_new)
+        B = len(seq_ids) if not a.device else seq_ids.numel()
+        kshape = (B, n_tok, self.n_head_kv, self.head_dim)
+        err = ErrBuf()
+        return check(lib().vxg_attn_cuda_f32_append(
+            self.ctx.h, self.h, B, n_tok, a.ptr(seq_ids, np.int32, (B,), "seq_ids"),
+            a.ptr(pos, np.int32, (B,), "pos"), a.ptr(k_new, np.float32, kshape, "k_new"),
+            a.ptr(v_new, np.float32, kshape, "v_new"), a.memkind, a.stream(stream), err.buf,
+            err.cap), err)
+
+    def decode(self, seq_ids, pos, q, k_new=None, v_new=None, q_gate=None, scale=None,
+               max_ctx: int = 0, out=None, stream=None):
+        """Append (if k_new) then attend over [0, pos[b]]: returns out [B][n_head][head_dim]."""
+        a = _Args(q)
+        B = len(seq_ids) if not a.device else seq_ids.numel()
+        n_head = (q.size if not a.device else q.numel()) // (B * self.head_dim)
+        qshape = (B, n_head, self.head_dim)
+        if scale is None:
+            scale = 1.0 / math.sqrt(self.head_dim)
+        if out is None:
+            if a.device:
+                import torch
+                out = torch.empty(qshape, dtype=torch.float32, device=q.device)
+            else:
+                out = np.empty(qshape, np.float32)
+        kshape = (B, self.n_head_kv, self.head_dim)
+        err = ErrBuf()
+        self.last_rc = check(lib().vxg_attn_cuda_f32_decode(
+            self.ctx.h, self.h, B, n_head, a.ptr(seq_ids, np.int32, (B,), "seq_ids"),
+            a.ptr(pos, np.int32, (B,), "pos"), a.ptr(q, np.float32, qshape, "q"),
+            a.ptr(k_new, np.float32, kshape, "k_new"), a.ptr(v_new, np.float32, kshape, "v_new"),
+            a.ptr(q_gate, np.float32, qshape, "q_gate"), ctypes.c_float(scale), max_ctx,
+            a.ptr(out, np.float32, qshape, "out", writable=True), a.memkind, a.stream(stream),
+            err.buf, err.cap), err)
+        return out
+
+
+def step_full_gqa(ctx: Context, kv: KvF32Pool, seq: int, q_raw, k_cur, v_cur, q_norm, k_norm,
+                  gated_q: bool, n_head: int, n_head_kv: int, head_dim: int, pos: int,
+                  rope_dim: int, rope_freq_base: float, rope_neox: bool, eps: float,
+                  att_cat) -> int:
+    """Drop-in for step_full_gqa (llm_ops.rs:196-300), the fp32-KV operator, on host buffers:
+    k_cur is overwritten with the normed / RoPE'd key and att_cat with the output."""
+    a = _Args(q_raw)
+    if a.device:
+        raise TypeError("step_full_gqa takes host (numpy) buffers, as the reference does")
+    err = ErrBuf()
+    return check(lib().vxg_attn_cuda_step_full_gqa(
+        ctx.h, kv.h, seq, a.ptr(q_raw, np.float32, name="q_raw"),
+        a.ptr(k_cur, np.float32, (n_head_kv * head_dim,), "k_cur", writable=True),
+        a.ptr(v_cur, np.float32, (n_head_kv * head_dim,), "v_cur"),
+        a.ptr(q_norm, np.float32, (head_dim,), "q_norm"),
+        a.ptr(k_norm, np.float32, (head_dim,), "k_norm"), int(bool(gated_q)), n_head, n_head_kv,
+        head_dim, pos, rope_dim, ctypes.c_float(rope_freq_base), int(bool(rope_neox)),
+        ctypes.c_float(eps), a.ptr(att_cat, np.float32, (n_head * head_dim,), "att_cat",
+                                   writable=True), err.buf, err.cap), err)
+
+
 def lse_combine(ctx: Context, m, l, o, gate=None, out=None, stream=None):
     """Merge partials m,l [P][R], o [P][R][hd] -> out [R][hd] (optional sigmoid gate)."""
     a = _Args(o)

@@ -90,9 +90,12 @@ struct Kv {
   Ctx* ctx = nullptr;           // nullptr once the owning context has been destroyed
   int device = 0;
   uint32_t n_seq = 0, n_kv = 0, hd = 0, cap = 0;
+  bool f32 = false;             // fp32 K/V (KvCacheMode::Fp32) instead of Q8_0 blocks
   uint8_t* k = nullptr;
   uint8_t* v = nullptr;
-  size_t tok_bytes() const { return (size_t)n_kv * (hd / 32) * vxg::kBlk; }
+  size_t tok_bytes() const {
+    return f32 ? (size_t)n_kv * hd * sizeof(float) : (size_t)n_kv * (hd / 32) * vxg::kBlk;
+  }
   size_t seq_bytes() const { return (size_t)cap * tok_bytes(); }
 };
 
@@ -110,6 +113,16 @@ Kv& use_kv(Ctx& c, void* h) {
   Kv& kv = *static_cast<Kv*>(h);
   require(kv.device == c.device, VXG_ATTN_ERR_INVALID_OPTION,
           "the KV pool lives on another device than this context");
+  return kv;
+}
+Kv& use_q8(Ctx& c, void* h) {
+  Kv& kv = use_kv(c, h);
+  require(!kv.f32, VXG_ATTN_ERR_INVALID_OPTION, "this operation needs a Q8_0 KV pool");
+  return kv;
+}
+Kv& use_f32(Ctx& c, void* h) {
+  Kv& kv = use_kv(c, h);
+  require(kv.f32, VXG_ATTN_ERR_INVALID_OPTION, "this operation needs an fp32 KV pool");
   return kv;
 }
 
@@ -251,6 +264,7 @@ vxg::DecodeArgs decode_args(Kv& kv, uint32_t n_batch, uint32_t n_head, const int
   a.max_ctx = (int)((max_ctx == 0 || max_ctx > kv.cap) ? kv.cap : max_ctx);
   a.scale = scale;
   a.status = status;
+  a.kv_f32 = kv.f32 ? 1 : 0;
   return a;
 }
 
@@ -418,15 +432,15 @@ int vxg_attn_cuda_memcpy(void* ctx, void* dst, const void* src, size_t bytes, in
 }
 
 // ---------------------------------------------------------------- KV pool ----------------------
-void* vxg_attn_cuda_kv_create(void* ctx, uint32_t n_seq, uint32_t n_head_kv, uint32_t head_dim,
-                              uint32_t cap_tokens, char* err, size_t cap) {
+static void* kv_create(void* ctx, uint32_t n_seq, uint32_t n_head_kv, uint32_t head_dim,
+                       uint32_t cap_tokens, bool f32, char* err, size_t cap) {
   Kv* kv = nullptr;
   int rc = guarded(ctx, nullptr, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
     require(n_seq > 0 && n_head_kv > 0 && cap_tokens > 0, VXG_ATTN_ERR_INVALID_OPTION,
             "n_seq, n_head_kv and cap_tokens must be positive");
     require(head_dim > 0 && head_dim % 32 == 0, VXG_ATTN_ERR_UNSUPPORTED,
-            "Q8_0 KV needs head_dim % 32 == 0 (llm.rs:291)");
+            f32 ? "head_dim must be a multiple of 32" : "Q8_0 KV needs head_dim % 32 == 0 (llm.rs:291)");
     require(head_dim <= 256, VXG_ATTN_ERR_UNSUPPORTED, "head_dim above 256 is not supported");
     require((uint64_t)n_seq * cap_tokens < (1ull << 31), VXG_ATTN_ERR_INVALID_OPTION,
             "n_seq * cap_tokens too large");
@@ -438,6 +452,7 @@ void* vxg_attn_cuda_kv_create(void* ctx, uint32_t n_seq, uint32_t n_head_kv, uin
     kv->n_kv = n_head_kv;
     kv->hd = head_dim;
     kv->cap = cap_tokens;
+    kv->f32 = f32;
     const size_t bytes = (size_t)n_seq * kv->seq_bytes();
     check(cudaMalloc(&kv->k, bytes), "cudaMalloc K pool");
     check(cudaMalloc(&kv->v, bytes), "cudaMalloc V pool");
@@ -451,6 +466,16 @@ void* vxg_attn_cuda_kv_create(void* ctx, uint32_t n_seq, uint32_t n_head_kv, uin
     return nullptr;
   }
   return kv;
+}
+
+void* vxg_attn_cuda_kv_create(void* ctx, uint32_t n_seq, uint32_t n_head_kv, uint32_t head_dim,
+                              uint32_t cap_tokens, char* err, size_t cap) {
+  return kv_create(ctx, n_seq, n_head_kv, head_dim, cap_tokens, false, err, cap);
+}
+
+void* vxg_attn_cuda_kv_create_f32(void* ctx, uint32_t n_seq, uint32_t n_head_kv,
+                                  uint32_t head_dim, uint32_t cap_tokens, char* err, size_t cap) {
+  return kv_create(ctx, n_seq, n_head_kv, head_dim, cap_tokens, true, err, cap);
 }
 
 void vxg_attn_cuda_kv_destroy(void* h) {
@@ -590,7 +615,7 @@ int vxg_attn_cuda_q8_append(void* ctx, void* h, uint32_t n_batch, uint32_t n_tok
                             const float* v_new, int memkind, void* stream, char* err, size_t cap) {
   return guarded(ctx, stream, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
-    Kv& kv = use_kv(c, h);
+    Kv& kv = use_q8(c, h);
     if (n_batch == 0 || n_tok == 0) return VXG_ATTN_OK;
     require(seq_ids && pos && k_new && v_new, VXG_ATTN_ERR_NULL_PTR, "null input");
     const bool host = memkind == VXG_ATTN_MEM_HOST;
@@ -618,7 +643,7 @@ int vxg_attn_cuda_q8_decode(void* ctx, void* h, uint32_t n_batch, uint32_t n_hea
                             char* err, size_t cap) {
   return guarded(ctx, stream, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
-    Kv& kv = use_kv(c, h);
+    Kv& kv = use_q8(c, h);
     if (n_batch == 0) return VXG_ATTN_OK;
     require(seq_ids && pos && q && out, VXG_ATTN_ERR_NULL_PTR, "null input");
     require((k_new == nullptr) == (v_new == nullptr), VXG_ATTN_ERR_NULL_PTR,
@@ -662,7 +687,7 @@ int vxg_attn_cuda_q8_prefill(void* ctx, void* h, uint32_t n_batch, uint32_t n_to
                              float* out, int memkind, void* stream, char* err, size_t cap) {
   return guarded(ctx, stream, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
-    Kv& kv = use_kv(c, h);
+    Kv& kv = use_q8(c, h);
     if (n_batch == 0 || n_tok == 0) return VXG_ATTN_OK;
     require(seq_ids && pos && q && k_new && v_new && out, VXG_ATTN_ERR_NULL_PTR, "null input");
     require(dtype == VXG_ATTN_DTYPE_F32 || dtype == VXG_ATTN_DTYPE_BF16,
@@ -729,6 +754,78 @@ int vxg_attn_cuda_q8_prefill(void* ctx, void* h, uint32_t n_batch, uint32_t n_to
   });
 }
 
+int vxg_attn_cuda_f32_append(void* ctx, void* h, uint32_t n_batch, uint32_t n_tok,
+                             const int32_t* seq_ids, const int32_t* pos, const float* k_new,
+                             const float* v_new, int memkind, void* stream, char* err,
+                             size_t cap) {
+  return guarded(ctx, stream, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    Kv& kv = use_f32(c, h);
+    if (n_batch == 0 || n_tok == 0) return VXG_ATTN_OK;
+    require(seq_ids && pos && k_new && v_new, VXG_ATTN_ERR_NULL_PTR, "null input");
+    const bool host = memkind == VXG_ATTN_MEM_HOST;
+    if (host) check_host_positions(kv, n_batch, seq_ids, pos, n_tok);
+    cudaStream_t st = pick_stream(c, stream);
+    const size_t kvd = (size_t)n_batch * n_tok * kv.n_kv * kv.hd * sizeof(float);
+    Stager sg(c, st, host);
+    sg.in(seq_ids, n_batch * sizeof(int32_t));
+    sg.in(pos, n_batch * sizeof(int32_t));
+    sg.in(k_new, kvd);
+    sg.in(v_new, kvd);
+    sg.upload();
+    check(vxg::launch_f32_append(seq_ids, pos, k_new, v_new, reinterpret_cast<float*>(kv.k),
+                                 reinterpret_cast<float*>(kv.v), (int)n_batch, (int)n_tok,
+                                 (int)kv.n_seq, (int)kv.cap, (int)kv.n_kv, (int)kv.hd,
+                                 c.d_status, st),
+          "f32 append launch");
+    return finish(c, stream, st);
+  });
+}
+
+int vxg_attn_cuda_f32_decode(void* ctx, void* h, uint32_t n_batch, uint32_t n_head,
+                             const int32_t* seq_ids, const int32_t* pos, const float* q,
+                             const float* k_new, const float* v_new, const float* q_gate,
+                             float scale, uint32_t max_ctx, float* out, int memkind, void* stream,
+                             char* err, size_t cap) {
+  return guarded(ctx, stream, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    Kv& kv = use_f32(c, h);
+    if (n_batch == 0) return VXG_ATTN_OK;
+    require(seq_ids && pos && q && out, VXG_ATTN_ERR_NULL_PTR, "null input");
+    require((k_new == nullptr) == (v_new == nullptr), VXG_ATTN_ERR_NULL_PTR,
+            "k_new and v_new must both be given or both be NULL");
+    check_decode_shape(kv, n_batch, n_head);
+    const bool host = memkind == VXG_ATTN_MEM_HOST;
+    if (host) check_host_positions(kv, n_batch, seq_ids, pos, 1);
+    cudaStream_t st = pick_stream(c, stream);
+    const size_t qb = (size_t)n_batch * n_head * kv.hd * sizeof(float);
+    const size_t kvd = (size_t)n_batch * kv.n_kv * kv.hd * sizeof(float);
+    Stager sg(c, st, host);
+    sg.in(seq_ids, n_batch * sizeof(int32_t));
+    sg.in(pos, n_batch * sizeof(int32_t));
+    sg.in(q, qb);
+    sg.in(k_new, kvd);
+    sg.in(v_new, kvd);
+    sg.in(q_gate, qb);
+    sg.out(out, qb);
+    sg.upload();
+    if (k_new)
+      check(vxg::launch_f32_append(seq_ids, pos, k_new, v_new, reinterpret_cast<float*>(kv.k),
+                                   reinterpret_cast<float*>(kv.v), (int)n_batch, 1,
+                                   (int)kv.n_seq, (int)kv.cap, (int)kv.n_kv, (int)kv.hd,
+                                   c.d_status, st),
+            "f32 append launch");
+    vxg::DecodeArgs a = decode_args(kv, n_batch, n_head, seq_ids, nullptr, pos, 1, q, scale,
+                                    max_ctx, c.d_status);
+    vxg::Partials p = carve_partials(c, a);
+    cudaEvent_t e0, e1;
+    record_timing(c, &e0, &e1);
+    check(vxg::launch_decode(a, p, q_gate, out, c.sm_count, 1, st, e0, e1), "decode launch");
+    sg.download();
+    return finish(c, stream, st);
+  });
+}
+
 int vxg_attn_cuda_q8_decode_partial(void* ctx, void* h, uint32_t n_batch, uint32_t n_head,
                                     const int32_t* seq_ids, const int32_t* kv_begin,
                                     const int32_t* kv_end, const float* q, float scale,
@@ -736,7 +833,7 @@ int vxg_attn_cuda_q8_decode_partial(void* ctx, void* h, uint32_t n_batch, uint32
                                     void* stream, char* err, size_t cap) {
   return guarded(ctx, stream, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
-    Kv& kv = use_kv(c, h);
+    Kv& kv = use_q8(c, h);
     if (n_batch == 0) return VXG_ATTN_OK;
     require(seq_ids && kv_begin && kv_end && q && m && l && o, VXG_ATTN_ERR_NULL_PTR,
             "null input");
@@ -829,7 +926,7 @@ int vxg_attn_cuda_step_full_gqa_q8(void* ctx, void* h, uint32_t seq, const float
                                    size_t cap) {
   return guarded(ctx, nullptr, err, cap, [&] {
     Ctx& c = use_ctx(ctx);
-    Kv& kv = use_kv(c, h);
+    Kv& kv = use_q8(c, h);
     require(q_raw && k_cur && v_cur && attn_out, VXG_ATTN_ERR_NULL_PTR, "null input");
     require(n_head_kv == kv.n_kv && head_dim == kv.hd, VXG_ATTN_ERR_INVALID_OPTION,
             "n_head_kv / head_dim differ from the KV pool's");
@@ -892,6 +989,87 @@ int vxg_attn_cuda_step_full_gqa_q8(void* ctx, void* h, uint32_t seq, const float
     vxg::Partials p = carve_partials(c, a);
     float* dout = reinterpret_cast<float*>(base + o_out);
     check(vxg::launch_decode(a, p, dg, dout, c.sm_count, c.force_generic, st, nullptr, nullptr),
+          "decode launch");
+    check(cudaMemcpyAsync(attn_out, dout, n_head * hdb, cudaMemcpyDeviceToHost, st), "download");
+    check(cudaMemcpyAsync(k_cur, dk, n_head_kv * hdb, cudaMemcpyDeviceToHost, st), "download k");
+    return collect_status(c, st);
+  });
+}
+
+int vxg_attn_cuda_step_full_gqa(void* ctx, void* h, uint32_t seq, const float* q_raw,
+                                float* k_cur, const float* v_cur, const float* q_norm,
+                                const float* k_norm, int gated_q, uint32_t n_head,
+                                uint32_t n_head_kv, uint32_t head_dim, uint32_t pos,
+                                uint32_t rope_dim, float rope_freq_base, int rope_neox, float eps,
+                                float* att_cat, char* err, size_t cap) {
+  const uint32_t rope_pos = pos;  // step_full_gqa ropes at the cache position (llm_ops.rs:235-251)
+  float* attn_out = att_cat;
+  return guarded(ctx, nullptr, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    Kv& kv = use_f32(c, h);
+    require(q_raw && k_cur && v_cur && attn_out, VXG_ATTN_ERR_NULL_PTR, "null input");
+    require(n_head_kv == kv.n_kv && head_dim == kv.hd, VXG_ATTN_ERR_INVALID_OPTION,
+            "n_head_kv / head_dim differ from the KV pool's");
+    check_decode_shape(kv, 1, n_head);
+    require(seq < kv.n_seq, VXG_ATTN_ERR_INVALID_OPTION, "sequence id out of range");
+    require(pos < kv.cap, VXG_ATTN_ERR_BUFFER_TOO_SMALL,
+            "position beyond the KV capacity (grow it with vxg_attn_cuda_kv_reserve)");
+    cudaStream_t st = c.stream;
+    // RoPE table with the C library, as apply_rope does (llm_ops.rs:81-101)
+    const uint32_t rdim = rope_dim < head_dim ? rope_dim : head_dim;
+    const uint32_t half = rdim / 2;
+    std::vector<float> cs(2 * (size_t)(half ? half : 1));
+    for (uint32_t i = 0; i < half; ++i) {
+      volatile float e = -(2.0f * (float)i) / (float)rdim;
+      const float freq = powf(rope_freq_base, e);
+      const float theta = (float)rope_pos * freq;
+      cs[2 * i] = cosf(theta);
+      cs[2 * i + 1] = sinf(theta);
+    }
+    const size_t hdb = head_dim * sizeof(float);
+    const size_t qraw_b = (size_t)n_head * (gated_q ? 2 : 1) * hdb;
+    Carver cv;
+    const size_t o_qraw = cv.take(qraw_b), o_k = cv.take(n_head_kv * hdb),
+                 o_v = cv.take(n_head_kv * hdb), o_qn = cv.take(hdb), o_kn = cv.take(hdb),
+                 o_cs = cv.take(cs.size() * sizeof(float)), o_q = cv.take(n_head * hdb),
+                 o_g = cv.take(n_head * hdb), o_out = cv.take(n_head * hdb),
+                 o_ids = cv.take(2 * sizeof(int32_t));
+    c.aux.reserve(cv.off, "cudaMalloc step buffers");
+    uint8_t* base = static_cast<uint8_t*>(c.aux.p);
+    auto up = [&](size_t off, const void* src, size_t bytes) {
+      check(cudaMemcpyAsync(base + off, src, bytes, cudaMemcpyHostToDevice, st), "upload");
+    };
+    up(o_qraw, q_raw, qraw_b);
+    up(o_k, k_cur, n_head_kv * hdb);
+    up(o_v, v_cur, n_head_kv * hdb);
+    if (q_norm) up(o_qn, q_norm, hdb);
+    if (k_norm) up(o_kn, k_norm, hdb);
+    if (half) up(o_cs, cs.data(), cs.size() * sizeof(float));
+    const int32_t ids[2] = {(int32_t)seq, (int32_t)pos};
+    up(o_ids, ids, sizeof(ids));
+    float* dk = reinterpret_cast<float*>(base + o_k);
+    float* dq = reinterpret_cast<float*>(base + o_q);
+    float* dg = gated_q ? reinterpret_cast<float*>(base + o_g) : nullptr;
+    check(vxg::launch_gqa_prep(reinterpret_cast<const float*>(base + o_qraw), dk,
+                               q_norm ? reinterpret_cast<const float*>(base + o_qn) : nullptr,
+                               k_norm ? reinterpret_cast<const float*>(base + o_kn) : nullptr,
+                               gated_q ? 1 : 0, (int)n_head, (int)n_head_kv, (int)head_dim,
+                               reinterpret_cast<const float2*>(base + o_cs), (int)half,
+                               rope_neox ? 1 : 0, eps, dq, dg, st),
+          "prep launch");
+    const int32_t* d_seq = reinterpret_cast<const int32_t*>(base + o_ids);
+    const int32_t* d_pos = d_seq + 1;
+    check(vxg::launch_f32_append(d_seq, d_pos, dk, reinterpret_cast<const float*>(base + o_v),
+                                 reinterpret_cast<float*>(kv.k), reinterpret_cast<float*>(kv.v),
+                                 1, 1, (int)kv.n_seq, (int)kv.cap, (int)kv.n_kv, (int)kv.hd,
+                                 c.d_status, st),
+          "f32 append launch");
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    vxg::DecodeArgs a = decode_args(kv, 1, n_head, d_seq, nullptr, d_pos, 1, dq, scale, pos + 1,
+                                    c.d_status);
+    vxg::Partials p = carve_partials(c, a);
+    float* dout = reinterpret_cast<float*>(base + o_out);
+    check(vxg::launch_decode(a, p, dg, dout, c.sm_count, 1, st, nullptr, nullptr),
           "decode launch");
     check(cudaMemcpyAsync(attn_out, dout, n_head * hdb, cudaMemcpyDeviceToHost, st), "download");
     check(cudaMemcpyAsync(k_cur, dk, n_head_kv * hdb, cudaMemcpyDeviceToHost, st), "download k");

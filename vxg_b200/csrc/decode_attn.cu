@@ -32,7 +32,9 @@ constexpr int kGenChunk = 512;  // tokens per split in the generic kernel
 // =============================================================================================
 // Generic split kernel
 // =============================================================================================
-template <int NB, int HPC>
+// F32: the cache holds fp32 K/V [n_seq][cap][n_kv][hd] (the reference's KvCacheMode::Fp32
+// vectors, llm_ops.rs:256-258) instead of Q8 blocks.
+template <int NB, int HPC, bool F32>
 __global__ void __launch_bounds__(128) decode_generic_split(DecodeArgs a, Partials part,
                                                             int max_split) {
   constexpr int HD = NB * 32;
@@ -52,6 +54,8 @@ __global__ void __launch_bounds__(128) decode_generic_split(DecodeArgs a, Partia
   const size_t seq_base = (size_t)s * a.cap * per_tok;
   const uint8_t* kb = a.k_pool + (seq_base + (size_t)kh * NB) * kBlk;
   const uint8_t* vb = a.v_pool + (seq_base + (size_t)kh * NB) * kBlk;
+  const float* kf = reinterpret_cast<const float*>(a.k_pool) + (seq_base + (size_t)kh * NB) * 32;
+  const float* vf = reinterpret_cast<const float*>(a.v_pool) + (seq_base + (size_t)kh * NB) * 32;
 
   float qv[HPC][NB];
 #pragma unroll
@@ -70,15 +74,25 @@ __global__ void __launch_bounds__(128) decode_generic_split(DecodeArgs a, Partia
   // chunks j, j + gridDim.x, ... of this entry all fold into this CTA's running state
   for (int t0 = beg + j * kGenChunk; t0 < end; t0 += gridDim.x * kGenChunk)
   for (int t = t0 + warp, t1 = min(end, t0 + kGenChunk); t < t1; t += 4) {
-    const uint8_t* kr = kb + (size_t)t * per_tok * kBlk;
-    const uint8_t* vr = vb + (size_t)t * per_tok * kBlk;
     float kx[NB], vx[NB];
+    if constexpr (F32) {
+      const float* kr = kf + (size_t)t * per_tok * 32;
+      const float* vr = vf + (size_t)t * per_tok * 32;
 #pragma unroll
-    for (int c = 0; c < NB; ++c) {
-      const float kd = f16bits_to_f32(*reinterpret_cast<const uint16_t*>(kr + c * kBlk));
-      const float vd = f16bits_to_f32(*reinterpret_cast<const uint16_t*>(vr + c * kBlk));
-      kx[c] = (float)(int8_t)kr[c * kBlk + 2 + lane] * kd;
-      vx[c] = (float)(int8_t)vr[c * kBlk + 2 + lane] * vd;
+      for (int c = 0; c < NB; ++c) {
+        kx[c] = kr[c * 32 + lane];
+        vx[c] = vr[c * 32 + lane];
+      }
+    } else {
+      const uint8_t* kr = kb + (size_t)t * per_tok * kBlk;
+      const uint8_t* vr = vb + (size_t)t * per_tok * kBlk;
+#pragma unroll
+      for (int c = 0; c < NB; ++c) {
+        const float kd = f16bits_to_f32(*reinterpret_cast<const uint16_t*>(kr + c * kBlk));
+        const float vd = f16bits_to_f32(*reinterpret_cast<const uint16_t*>(vr + c * kBlk));
+        kx[c] = (float)(int8_t)kr[c * kBlk + 2 + lane] * kd;
+        vx[c] = (float)(int8_t)vr[c * kBlk + 2 + lane] * vd;
+      }
     }
 #pragma unroll
     for (int g = 0; g < HPC; ++g) {
@@ -880,7 +894,7 @@ __global__ void __launch_bounds__(256) lse_combine_kernel(int n_parts, int n_row
 // =============================================================================================
 namespace {
 bool fast_applies(const DecodeArgs& a) {
-  return a.nb == fast::NB && a.n_kv == fast::NKV && a.n_head == fast::NKV * fast::G &&
+  return !a.kv_f32 && a.nb == fast::NB && a.n_kv == fast::NKV && a.n_head == fast::NKV * fast::G &&
          a.n_batch <= fast::MAXB;  // (and at most 512 SMs: the combine stages their ranges)
 }
 int heads_per_cta(int G) {
@@ -888,15 +902,15 @@ int heads_per_cta(int G) {
   while (hpc > 1 && G % hpc) hpc >>= 1;
   return hpc;
 }
-template <int NB>
+template <int NB, bool F32>
 cudaError_t launch_generic_nb(const DecodeArgs& a, const Partials& p, int max_split, int hpc,
                               cudaStream_t st) {
   dim3 grid(max_split, a.n_head / hpc, a.n_batch);
   switch (hpc) {
-    case 8: decode_generic_split<NB, 8><<<grid, 128, 0, st>>>(a, p, max_split); break;
-    case 4: decode_generic_split<NB, 4><<<grid, 128, 0, st>>>(a, p, max_split); break;
-    case 2: decode_generic_split<NB, 2><<<grid, 128, 0, st>>>(a, p, max_split); break;
-    default: decode_generic_split<NB, 1><<<grid, 128, 0, st>>>(a, p, max_split); break;
+    case 8: decode_generic_split<NB, 8, F32><<<grid, 128, 0, st>>>(a, p, max_split); break;
+    case 4: decode_generic_split<NB, 4, F32><<<grid, 128, 0, st>>>(a, p, max_split); break;
+    case 2: decode_generic_split<NB, 2, F32><<<grid, 128, 0, st>>>(a, p, max_split); break;
+    default: decode_generic_split<NB, 1, F32><<<grid, 128, 0, st>>>(a, p, max_split); break;
   }
   return cudaGetLastError();
 }
@@ -981,15 +995,28 @@ static cudaError_t run_split(const DecodeArgs& a, const Partials& p, int sm_coun
   *mode = 0;
   *max_split = generic_max_split(a);
   const int hpc = heads_per_cta(a.n_head / a.n_kv);
+  if (a.kv_f32) {
+    switch (a.nb) {
+      case 1: return launch_generic_nb<1, true>(a, p, *max_split, hpc, st);
+      case 2: return launch_generic_nb<2, true>(a, p, *max_split, hpc, st);
+      case 3: return launch_generic_nb<3, true>(a, p, *max_split, hpc, st);
+      case 4: return launch_generic_nb<4, true>(a, p, *max_split, hpc, st);
+      case 5: return launch_generic_nb<5, true>(a, p, *max_split, hpc, st);
+      case 6: return launch_generic_nb<6, true>(a, p, *max_split, hpc, st);
+      case 7: return launch_generic_nb<7, true>(a, p, *max_split, hpc, st);
+      case 8: return launch_generic_nb<8, true>(a, p, *max_split, hpc, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (a.nb) {
-    case 1: return launch_generic_nb<1>(a, p, *max_split, hpc, st);
-    case 2: return launch_generic_nb<2>(a, p, *max_split, hpc, st);
-    case 3: return launch_generic_nb<3>(a, p, *max_split, hpc, st);
-    case 4: return launch_generic_nb<4>(a, p, *max_split, hpc, st);
-    case 5: return launch_generic_nb<5>(a, p, *max_split, hpc, st);
-    case 6: return launch_generic_nb<6>(a, p, *max_split, hpc, st);
-    case 7: return launch_generic_nb<7>(a, p, *max_split, hpc, st);
-    case 8: return launch_generic_nb<8>(a, p, *max_split, hpc, st);
+    case 1: return launch_generic_nb<1, false>(a, p, *max_split, hpc, st);
+    case 2: return launch_generic_nb<2, false>(a, p, *max_split, hpc, st);
+    case 3: return launch_generic_nb<3, false>(a, p, *max_split, hpc, st);
+    case 4: return launch_generic_nb<4, false>(a, p, *max_split, hpc, st);
+    case 5: return launch_generic_nb<5, false>(a, p, *max_split, hpc, st);
+    case 6: return launch_generic_nb<6, false>(a, p, *max_split, hpc, st);
+    case 7: return launch_generic_nb<7, false>(a, p, *max_split, hpc, st);
+    case 8: return launch_generic_nb<8, false>(a, p, *max_split, hpc, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -17,6 +17,13 @@ cudaError_t launch_q8_append_bf16(const int32_t* seq_ids, const int32_t* pos, co
                                   int n_tok, int n_seq, int cap, int n_kv, int nb, uint32_t* status,
                                   cudaStream_t stream);
 
+// Copy of fp32 K/V tokens into fp32 pools: k_new/v_new[b][t][n_kv][hd] -> sequence seq_ids[b]
+// at position pos[b] + t (the reference's k_cache.extend_from_slice, llm_ops.rs:256-257).
+cudaError_t launch_f32_append(const int32_t* seq_ids, const int32_t* pos, const float* k_new,
+                              const float* v_new, float* k_pool, float* v_pool, int n_batch,
+                              int n_tok, int n_seq, int cap, int n_kv, int hd, uint32_t* status,
+                              cudaStream_t stream);
+
 // decode_attn.cu ---------------------------------------------------------------------------
 struct DecodeArgs {
   const int32_t* seq_ids;  // [n_batch]
@@ -30,6 +37,7 @@ struct DecodeArgs {
   int max_ctx;             // upper bound of (end - begin) over the batch (host-known)
   float scale;             // softmax scale (1/sqrt(hd) in the reference)
   uint32_t* status;
+  int kv_f32;              // pools hold fp32 K/V [n_seq][cap][n_kv][hd] (portable kernel only)
 };
 
 // Partial (m, l, o) buffers for the split-KV pass: m, l in log2 units, o unnormalised.

@@ -85,4 +85,40 @@ cudaError_t launch_q8_append_bf16(const int32_t* seq_ids, const int32_t* pos, co
   return cudaGetLastError();
 }
 
+// fp32 pools: one thread per 4 floats of one (batch entry, token) row of K and of V.
+__global__ void __launch_bounds__(256) f32_append_kernel(const int32_t* __restrict__ seq_ids,
+                                                         const int32_t* __restrict__ pos,
+                                                         const float* __restrict__ k_new,
+                                                         const float* __restrict__ v_new,
+                                                         float* __restrict__ k_pool,
+                                                         float* __restrict__ v_pool, int n_batch,
+                                                         int n_tok, int n_seq, int cap, int row4,
+                                                         uint32_t* status) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long per = (long long)n_batch * n_tok * row4;
+  if (i >= per) return;
+  const int bt = (int)(i / row4), c = (int)(i - (long long)bt * row4);
+  const int b = bt / n_tok, t = bt - b * n_tok;
+  const int s = seq_ids[b], p = pos[b] + t;
+  if (s < 0 || s >= n_seq || p < 0 || p >= cap) {
+    if (c == 0) atomicOr(status, kStatusBadIndex);
+    return;
+  }
+  const size_t dst = ((size_t)s * cap + p) * row4 + c;
+  reinterpret_cast<float4*>(k_pool)[dst] = reinterpret_cast<const float4*>(k_new)[i];
+  reinterpret_cast<float4*>(v_pool)[dst] = reinterpret_cast<const float4*>(v_new)[i];
+}
+
+cudaError_t launch_f32_append(const int32_t* seq_ids, const int32_t* pos, const float* k_new,
+                              const float* v_new, float* k_pool, float* v_pool, int n_batch,
+                              int n_tok, int n_seq, int cap, int n_kv, int hd, uint32_t* status,
+                              cudaStream_t stream) {
+  const int row4 = n_kv * hd / 4;
+  const long long n = (long long)n_batch * n_tok * row4;
+  if (n == 0) return cudaSuccess;
+  f32_append_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+      seq_ids, pos, k_new, v_new, k_pool, v_pool, n_batch, n_tok, n_seq, cap, row4, status);
+  return cudaGetLastError();
+}
+
 }  // namespace vxg
