@@ -341,7 +341,7 @@ def run_deltanet(args, world, rank, local):
         "config": {"workload": "config4: DeltaNet decode, 64 seqs x 32 heads, dk=dv=128, fp32 "
                                "state N(0,0.02^2) read+written every step",
                    "l2": "state larger than L2 (268 MB per step)"},
-        "roofline": {"kernel": "deltanet_step_kernel", "bound": "hbm", "achieved": ach,
+        "roofline": {"kernel": "deltanet_step_persistent", "bound": "hbm", "achieved": ach,
                      "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": peak_kind,
                      "traffic": profile_traffic("deltanet_step_config4.json")},
         "gpu_launches": K, "clocks": sampler.summary(),

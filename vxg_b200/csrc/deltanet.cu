@@ -161,13 +161,14 @@ __global__ void __launch_bounds__(256) deltanet_step_kernel(DeltaNetArgs a) {
 // ---------------------------------------------------------------------------------------------
 namespace dn {
 constexpr int MAXE = 128 * 128;        // state floats per stage
+constexpr int NS = 3;                  // states in flight (3 x 64 KiB ring)
 constexpr uint64_t kWaitNs = 2000000000ull;
 struct __align__(128) Smem {
-  float state[2][MAXE];
-  float q[2][256], k[2][256], v[2][256];
+  float state[NS][MAXE];
+  float q[NS][256], k[NS][256], v[NS][256];
   float o[256];
   float red[8];
-  uint64_t full[2];
+  uint64_t full[NS];
 };
 }  // namespace dn
 
@@ -183,8 +184,7 @@ __global__ void __launch_bounds__(256, 1) deltanet_step_persistent(DeltaNetArgs 
   const int n_items = a.n_batch * a.n_vh;
   const uint32_t st_bytes = (uint32_t)a.dv * DK * 4;
   if (tid == 0) {
-    mbar_init(&sm.full[0], 1);
-    mbar_init(&sm.full[1], 1);
+    for (int i = 0; i < dn::NS; ++i) mbar_init(&sm.full[i], 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -198,15 +198,14 @@ __global__ void __launch_bounds__(256, 1) deltanet_step_persistent(DeltaNetArgs 
     bulk_g2s(sm.k[buf], a.k + (size_t)b * a.k_bs + (size_t)hk * DK, qb, &sm.full[buf]);
     bulk_g2s(sm.v[buf], a.v + (size_t)b * a.v_bs + (size_t)h * a.dv, vb, &sm.full[buf]);
   };
-  if (tid == 0) {
-    if ((int)blockIdx.x < n_items) issue(blockIdx.x, 0);
-    if ((int)(blockIdx.x + gridDim.x) < n_items) issue(blockIdx.x + gridDim.x, 1);
-  }
+  if (tid == 0)
+    for (int i = 0; i < dn::NS; ++i)
+      if ((int)(blockIdx.x + i * gridDim.x) < n_items) issue(blockIdx.x + i * gridDim.x, i);
   bool bad = false;
   int it = 0;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
-    const int buf = it & 1;
-    const uint32_t par = (uint32_t)(it >> 1) & 1u;
+    const int buf = it % dn::NS;
+    const uint32_t par = (uint32_t)(it / dn::NS) & 1u;
     const int b = item / a.n_vh, h = item - b * a.n_vh;
     const size_t gi = (size_t)b * a.g_bs + h;
     const float beta = sigmoidf_(a.beta_raw[gi]);
@@ -214,7 +213,10 @@ __global__ void __launch_bounds__(256, 1) deltanet_step_persistent(DeltaNetArgs 
     const bool ok = __syncthreads_and(mbar_wait(&sm.full[buf], par, dn::kWaitNs));
     if (!ok) {
       if (tid == 0) atomicOr(a.status, kStatusTimeout);
-      mbar_wait(&sm.full[buf ^ 1], ((it + 1) >> 1) & 1u, dn::kWaitNs);
+      // let the copies already in flight land before the CTA leaves
+      for (int k = 1; k < dn::NS; ++k)
+        if (item + k * (int)gridDim.x < n_items)
+          mbar_wait(&sm.full[(it + k) % dn::NS], (uint32_t)((it + k) / dn::NS) & 1u, dn::kWaitNs);
       return;
     }
     float4 qv[V4], kv[V4];
@@ -273,7 +275,7 @@ __global__ void __launch_bounds__(256, 1) deltanet_step_persistent(DeltaNetArgs 
       }
     }
     __syncthreads();  // everyone is done with this stage (and sm.o is complete)
-    if (tid == 0 && item + 2 * (int)gridDim.x < n_items) issue(item + 2 * gridDim.x, buf);
+    if (tid == 0 && item + dn::NS * (int)gridDim.x < n_items) issue(item + dn::NS * gridDim.x, buf);
     if (a.y) {
       float part = 0.f;
       for (int j = tid; j < a.dv; j += 256) part = fmaf(sm.o[j], sm.o[j], part);
