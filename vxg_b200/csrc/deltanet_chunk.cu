@@ -5,14 +5,13 @@
 // w_t = beta_t (v_t - g_t S_{t-1} k_t); then S_t = g_t S_{t-1} + w_t k_t^T, and over a chunk of
 // C tokens with cumulative log decay L_t = sum_{i<=t} log g_i (gamma_t = exp L_t):
 //   A[t][i] = beta_t exp(L_t - L_i) (k_t . k_i)   (i < t),   T = (I + A)^-1
-//   U  = T diag(beta) V,   Wk = T diag(beta gamma) K            (chunk-local)
-//   W  = U - Wk S0^T                                            (rows w_t of the chunk)
+//   W  = T diag(beta) (V - diag(gamma) K S0^T)                  (rows w_t of the chunk)
 //   O  = diag(gamma) Q S0^T + (M o Q K^T) W,   M[t][i] = exp(L_t - L_i) for i <= t
 //   S_C = gamma_C S0 + W^T diag(exp(L_C - L)) K
 // which is the same recurrence re-associated.  One CTA = (sequence, v head, 64 rows of the
 // state), chunks in order, state rows on chip.  The products run on mma.sync m16n8k8 TF32 with
 // f32 accumulation; the triangular solve's products and the state update use 3xTF32 (hi/lo
-// operand splits), which keeps the result within ~4% of the 1e-3 bar of the sequential fp32
+// operand splits), which keeps the result within a few % of the 1e-3 bar of the sequential fp32
 // recurrence at 8192 tokens (the single-pass products contribute that; the state update and
 // the solve would otherwise dominate).
 #include "kernels.h"
@@ -24,9 +23,11 @@ constexpr int C = 64;        // chunk length
 constexpr int DK = 128;
 constexpr int DS = 64;       // state rows (v dims) per CTA
 constexpr int THREADS = 256;
-constexpr int LDK = DK + 4;  // row stride of K, Q, S (floats): 4 mod 32
-constexpr int LDR = DS + DK + 8;  // R / X = [beta V | beta gamma K] -> [U | Wk] -> [W | Wk]
-constexpr int LDA = C + 4;
+// Row strides (floats).  Matrices read along k (contiguous) take 64-bit fragment loads and want
+// a stride of 8 mod 32; R, read along its rows by most products, wants 4 mod 32.
+constexpr int LDK = DK + 8;       // K, Q, S
+constexpr int LDR = DS + 4;       // R: V rows -> right-hand side -> W
+constexpr int LDA = C + 8;        // A / T, P
 
 struct __align__(16) Smem {
   float k[C][LDK];
@@ -41,11 +42,6 @@ struct __align__(16) Smem {
   float rdec[C];     // exp(L_C - L_t)
 };
 
-__device__ __forceinline__ uint32_t tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
 __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {
   asm volatile(
@@ -54,35 +50,80 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// f32 -> (hi, lo) with hi the top 19 bits (what the TF32 datapath reads) and lo = x - hi exact
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = __float_as_uint(x) & 0xFFFFE000u;
+  lo = __float_as_uint(x - __uint_as_float(hi));
+}
 
-// acc[nt] (+)= A(m0.., k) B(k, n0 + 8 nt ..) over k in [k0, k1), one 16-row tile, NT 8-col tiles.
-// fa(m, k) / fb(k, n) read the operands (f32); X3 adds the hi/lo correction products.
-template <int NT, bool X3, class FA, class FB>
-__device__ __forceinline__ void warp_mma(float (&acc)[NT][4], int m0, int n0, int k0, int k1,
-                                         FA fa, FB fb) {
+// acc[nt] (+)= A(m0.., k) B(k, n0 + 8 nt ..) over k in [k0, k1): one 16-row tile, NT 8-col
+// tiles.  A is [m][k] (AK) or [k][m]; B is [n][k] (BK) or [k][n]; ascale (optional) scales A's
+// column k.  Operands go to the TF32 datapath as raw f32 bits (it reads the top 19); X3 adds the
+// hi/lo correction products.  Inside each 8-wide k step, fragment slot q holds k + 2q and slot
+// q + 4 holds k + 2q + 1 (the same permutation for A and B), so k-contiguous operands load as
+// 64-bit pairs.
+template <int NT, bool X3, bool AK, bool BK>
+__device__ __forceinline__ void warp_mma(float (&acc)[NT][4], const float* A, int lda,
+                                         const float* B, int ldb, int m0, int n0, int k0, int k1,
+                                         const float* ascale = nullptr) {
   const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  // the two correction products accumulate separately: three short dependency chains per tile
+  float c1[X3 ? NT : 1][4], c2[X3 ? NT : 1][4];
+#pragma unroll
+  for (int i = 0; i < (X3 ? NT : 1); ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c1[i][e] = c2[i][e] = 0.f;
   for (int k = k0; k < k1; k += 8) {
-    const float af[4] = {fa(m0 + g, k + q), fa(m0 + g + 8, k + q), fa(m0 + g, k + q + 4),
-                         fa(m0 + g + 8, k + q + 4)};
+    const int kk = k + 2 * q;
+    float a[4];
+    if constexpr (AK) {
+      const float2 r0 = *reinterpret_cast<const float2*>(A + (m0 + g) * lda + kk);
+      const float2 r1 = *reinterpret_cast<const float2*>(A + (m0 + g + 8) * lda + kk);
+      a[0] = r0.x; a[2] = r0.y; a[1] = r1.x; a[3] = r1.y;
+    } else {
+      a[0] = A[kk * lda + m0 + g];
+      a[2] = A[(kk + 1) * lda + m0 + g];
+      a[1] = A[kk * lda + m0 + g + 8];
+      a[3] = A[(kk + 1) * lda + m0 + g + 8];
+    }
+    if (ascale) {
+      const float s0 = ascale[kk], s1 = ascale[kk + 1];
+      a[0] *= s0; a[1] *= s0; a[2] *= s1; a[3] *= s1;
+    }
     uint32_t ah[4], al[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      ah[i] = tf32(af[i]);
-      if constexpr (X3) al[i] = tf32(af[i] - __uint_as_float(ah[i]));
+      if constexpr (X3) split_tf32(a[i], ah[i], al[i]);
+      else ah[i] = __float_as_uint(a[i]);
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int n = n0 + 8 * nt + g;
-      const float b0 = fb(k + q, n), b1 = fb(k + q + 4, n);
-      const uint32_t bh0 = tf32(b0), bh1 = tf32(b1);
-      if constexpr (X3) {
-        const uint32_t bl0 = tf32(b0 - __uint_as_float(bh0)), bl1 = tf32(b1 - __uint_as_float(bh1));
-        mma_tf32(acc[nt], al, bh0, bh1);
-        mma_tf32(acc[nt], ah, bl0, bl1);
+      float b0, b1;
+      if constexpr (BK) {
+        const float2 r = *reinterpret_cast<const float2*>(B + n * ldb + kk);
+        b0 = r.x; b1 = r.y;
+      } else {
+        b0 = B[kk * ldb + n];
+        b1 = B[(kk + 1) * ldb + n];
       }
-      mma_tf32(acc[nt], ah, bh0, bh1);
+      if constexpr (X3) {
+        uint32_t bh0, bl0, bh1, bl1;
+        split_tf32(b0, bh0, bl0);
+        split_tf32(b1, bh1, bl1);
+        mma_tf32(c1[nt], al, bh0, bh1);
+        mma_tf32(c2[nt], ah, bl0, bl1);
+        mma_tf32(acc[nt], ah, bh0, bh1);
+      } else {
+        mma_tf32(acc[nt], ah, __float_as_uint(b0), __float_as_uint(b1));
+      }
     }
   }
+  if constexpr (X3)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[nt][e] += c1[nt][e] + c2[nt][e];
 }
 
 template <int NT>
@@ -120,24 +161,63 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
     const int t0 = c * C;
     __syncthreads();  // previous chunk's readers of k, q, r are done
     // ---- loads: K, Q (normalised), V slice (raw), beta, log decay -------------------------
-    for (int i = tid; i < C * DK / 4; i += THREADS) {
-      const int r = i / (DK / 4), c4 = (i % (DK / 4)) * 4;
-      const int t = t0 + r;
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
-      if (t < a.n_tok) {
-        const size_t off = (((size_t)b * a.n_tok + t) * a.n_kh + hk) * DK + c4;
-        kv = *reinterpret_cast<const float4*>(kn + off);
-        qv = *reinterpret_cast<const float4*>(qn + off);
+    {
+      // all loads first (one round trip), then the shared-memory stores
+      constexpr int NKQ = C * DK / 4 / THREADS, NV = C * DS / 4 / THREADS;
+      float4 kv[NKQ], qv[NKQ], vv[NV];
+#pragma unroll
+      for (int u = 0; u < NKQ; ++u) {
+        const int i = tid + u * THREADS, r = i / (DK / 4), c4 = (i % (DK / 4)) * 4;
+        const int t = t0 + r;
+        kv[u] = qv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < a.n_tok) {
+          const size_t off = (((size_t)b * a.n_tok + t) * a.n_kh + hk) * DK + c4;
+          kv[u] = *reinterpret_cast<const float4*>(kn + off);
+          qv[u] = *reinterpret_cast<const float4*>(qn + off);
+        }
       }
-      *reinterpret_cast<float4*>(&sm.k[r][c4]) = kv;
-      *reinterpret_cast<float4*>(&sm.q[r][c4]) = qv;
+#pragma unroll
+      for (int u = 0; u < NV; ++u) {
+        const int i = tid + u * THREADS, r = i / (DS / 4), j4 = (i % (DS / 4)) * 4;
+        const int t = t0 + r;
+        vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < a.n_tok)
+          vv[u] = *reinterpret_cast<const float4*>(a.v + (size_t)b * a.v_bs +
+                                                   (size_t)t * a.v_ts + (size_t)h * a.dv +
+                                                   sl * DS + j4);
+      }
+#pragma unroll
+      for (int u = 0; u < NKQ; ++u) {
+        const int i = tid + u * THREADS, r = i / (DK / 4), c4 = (i % (DK / 4)) * 4;
+        *reinterpret_cast<float4*>(&sm.k[r][c4]) = kv[u];
+        *reinterpret_cast<float4*>(&sm.q[r][c4]) = qv[u];
+      }
+#pragma unroll
+      for (int u = 0; u < NV; ++u) {
+        const int i = tid + u * THREADS, r = i / (DS / 4), j4 = (i % (DS / 4)) * 4;
+        *reinterpret_cast<float4*>(&sm.r[r][j4]) = vv[u];
+      }
     }
-    for (int i = tid; i < C * DS; i += THREADS) {
-      const int r = i / DS, j = i % DS;
-      const int t = t0 + r;
-      sm.r[r][j] = t < a.n_tok ? a.v[(size_t)b * a.v_bs + (size_t)t * a.v_ts +
-                                     (size_t)h * a.dv + sl * DS + j]
-                               : 0.f;
+    // the next chunk's rows go to L2 while this one computes
+    if (c + 1 < n_chunks) {
+      const int tn = t0 + C + (tid & 63);
+      if (tn < a.n_tok) {
+        const int part = tid >> 6;  // 4 threads per token row: K, Q halves, V, gates
+        const size_t off = (((size_t)b * a.n_tok + tn) * a.n_kh + hk) * DK;
+        const float* vrow = a.v + (size_t)b * a.v_bs + (size_t)tn * a.v_ts + (size_t)h * a.dv +
+                            sl * DS;
+        const size_t gi = ((size_t)b * a.n_tok + tn) * a.n_vh + h;
+        const void* p0 = part == 0 ? (const void*)(kn + off) : part == 1 ? (const void*)(qn + off)
+                       : part == 2 ? (const void*)vrow : (const void*)(lgs + gi);
+        const void* p1 = part == 0 ? (const void*)(kn + off + 64) : part == 1 ? (const void*)(qn + off + 64)
+                       : part == 2 ? (const void*)(vrow + 32) : (const void*)(gates + gi);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p0));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p1));
+        if (part < 2) {
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const float*>(p0) + 32));
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const float*>(p1) + 32));
+        }
+      }
     }
     if (warp == 0) {
       // inclusive scan of the log decays (two tokens per lane); padded tokens: beta 0, decay 1
@@ -162,21 +242,12 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
       sm.rdec[2 * lane + 1] = expf(LC - s);
     }
     __syncthreads();
-    // ---- right-hand sides: [beta V | beta gamma K]; G = K K^T -> A; Q K^T -> P -------------
-    for (int i = tid; i < C * DK; i += THREADS) {
-      const int r = i / DK, j = i % DK;
-      sm.r[r][DS + j] = sm.beta[r] * sm.gam[r] * sm.k[r][j];
-    }
-    for (int i = tid; i < C * DS; i += THREADS) {
-      const int r = i / DS, j = i % DS;
-      sm.r[r][j] *= sm.beta[r];
-    }
+    // ---- G = K K^T -> A;  RHS = beta (V - diag(gamma) K S0^T) over the V rows --------------
     {
       float acc[4][4];
       zero(acc);
-      warp_mma<4, false>(acc, 16 * mt, 32 * half, 0, DK,
-                         [&](int m, int k) { return sm.k[m][k]; },
-                         [&](int k, int n) { return sm.k[n][k]; });
+      warp_mma<4, false, true, true>(acc, &sm.k[0][0], LDK, &sm.k[0][0], LDK, 16 * mt,
+                                     32 * half, 0, DK);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
@@ -185,21 +256,20 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
           sm.a[t][i] = i < t ? sm.beta[t] * expf(sm.L[t] - sm.L[i]) * acc[nt][e] : 0.f;
         }
       zero(acc);
-      warp_mma<4, false>(acc, 16 * mt, 32 * half, 0, DK,
-                         [&](int m, int k) { return sm.q[m][k]; },
-                         [&](int k, int n) { return sm.k[n][k]; });
+      warp_mma<4, false, true, true>(acc, &sm.k[0][0], LDK, &sm.s[0][0], LDK, 16 * mt,
+                                     32 * half, 0, DK);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int t = 16 * mt + g + (e >> 1) * 8, i = 32 * half + 8 * nt + 2 * qd + (e & 1);
-          sm.p[t][i] = i <= t ? expf(sm.L[t] - sm.L[i]) * acc[nt][e] : 0.f;
+          const int t = 16 * mt + g + (e >> 1) * 8, j = 32 * half + 8 * nt + 2 * qd + (e & 1);
+          sm.r[t][j] = sm.beta[t] * (sm.r[t][j] - sm.gam[t] * acc[nt][e]);
         }
     }
     __syncthreads();
-    // ---- diagonal 16x16 blocks of T = (I + A)^-1, in place (lane j of a half-warp = column j)
-    if (warp < 2) {
-      const int blk = 2 * warp + (lane >> 4), j = lane & 15, o = 16 * blk;
+    if (warp < 4) {
+      // ---- diagonal 16x16 block `warp` of T = (I + A)^-1 in place; lane j = column j -------
+      const int j = lane & 15, o = 16 * warp;
       float col[16];
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
@@ -212,23 +282,36 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
         col[r] = v;
       }
       __syncwarp();
+      if (lane < 16)
 #pragma unroll
-      for (int r = 0; r < 16; ++r) sm.a[o + r][o + j] = col[r];
+        for (int r = 0; r < 16; ++r) sm.a[o + r][o + j] = col[r];
+    } else {
+      // ---- meanwhile P = M o Q K^T, one 16-row tile per warp ------------------------------------
+      const int m = warp - 4;
+      float acc[8][4];
+      zero(acc);
+      warp_mma<8, false, true, true>(acc, &sm.q[0][0], LDK, &sm.k[0][0], LDK, 16 * m, 0, 0, DK);
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = 16 * m + g + (e >> 1) * 8, i = 8 * nt + 2 * qd + (e & 1);
+          sm.p[t][i] = i <= t ? expf(sm.L[t] - sm.L[i]) * acc[nt][e] : 0.f;
+        }
     }
     __syncthreads();
-    // ---- blocked forward substitution X = (I + A)^-1 R, each warp owning 24 columns --------
-    {
-      const int n0 = 24 * warp;
+    float o1[8][4];  // warps 4-7: diag(gamma) Q S0^T of their 16-row tile, kept across the sync
+    if (warp < 4) {
+      // ---- W = (I + A)^-1 RHS by blocked forward substitution, warp w owning 16 columns ------
+      const int n0 = 16 * warp;
       for (int bi = 0; bi < 4; ++bi) {
-        float acc[3][4];
+        float acc[2][4];
         zero(acc);
         if (bi > 0)
-          warp_mma<3, true>(acc, 16 * bi, n0, 0, 16 * bi,
-                            [&](int m, int k) { return sm.a[m][k]; },
-                            [&](int k, int n) { return sm.r[k][n]; });
-        // Y = R_bi - sum_k A_bi,k X_k, written over R_bi (own columns)
+          warp_mma<2, true, true, false>(acc, &sm.a[0][0], LDA, &sm.r[0][0], LDR, 16 * bi, n0,
+                                         0, 16 * bi);
 #pragma unroll
-        for (int nt = 0; nt < 3; ++nt)
+        for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int t = 16 * bi + g + (e >> 1) * 8, n = n0 + 8 * nt + 2 * qd + (e & 1);
@@ -236,12 +319,11 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
           }
         __syncwarp();
         zero(acc);
-        warp_mma<3, true>(acc, 16 * bi, n0, 16 * bi, 16 * bi + 16,
-                          [&](int m, int k) { return sm.a[m][k]; },
-                          [&](int k, int n) { return sm.r[k][n]; });
+        warp_mma<2, true, true, false>(acc, &sm.a[0][0], LDA, &sm.r[0][0], LDR, 16 * bi, n0,
+                                       16 * bi, 16 * bi + 16);
         __syncwarp();
 #pragma unroll
-        for (int nt = 0; nt < 3; ++nt)
+        for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int t = 16 * bi + g + (e >> 1) * 8, n = n0 + 8 * nt + 2 * qd + (e & 1);
@@ -249,59 +331,40 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
           }
         __syncwarp();
       }
+    } else {
+      const int m = warp - 4;
+      zero(o1);
+      warp_mma<8, false, true, true>(o1, &sm.q[0][0], LDK, &sm.s[0][0], LDK, 16 * m, 0, 0, DK);
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o1[nt][e] *= sm.gam[16 * m + g + (e >> 1) * 8];
     }
-    __syncthreads();
-    // ---- W = U - Wk S0^T (in place over U) --------------------------------------------------
-    {
-      float acc[4][4];
-      zero(acc);
-      warp_mma<4, false>(acc, 16 * mt, 32 * half, 0, DK,
-                         [&](int m, int k) { return sm.r[m][DS + k]; },
-                         [&](int k, int n) { return sm.s[n][k]; });
+    __syncthreads();  // W complete; S0 no longer read
+    if (warp >= 4) {
+      // ---- O = diag(gamma) Q S0^T + P W -> global -------------------------------------------
+      const int m = warp - 4;
+      warp_mma<8, false, true, false>(o1, &sm.p[0][0], LDA, &sm.r[0][0], LDR, 16 * m, 0, 0,
+                                      16 * m + 16);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = 16 * mt + g + (e >> 1) * 8, j = 32 * half + 8 * nt + 2 * qd + (e & 1);
-          sm.r[t][j] -= acc[nt][e];
-        }
-    }
-    __syncthreads();
-    // ---- O = diag(gamma) Q S0^T + P W -> global ----------------------------------------------
-    {
-      float acc[4][4];
-      zero(acc);
-      warp_mma<4, false>(acc, 16 * mt, 32 * half, 0, DK,
-                         [&](int m, int k) { return sm.q[m][k]; },
-                         [&](int k, int n) { return sm.s[n][k]; });
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[nt][e] *= sm.gam[16 * mt + g + (e >> 1) * 8];
-      warp_mma<4, false>(acc, 16 * mt, 32 * half, 0, 16 * mt + 16,
-                         [&](int m, int k) { return sm.p[m][k]; },
-                         [&](int k, int n) { return sm.r[k][n]; });
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
-          const int t = t0 + 16 * mt + g + (e >> 1) * 8, j = 32 * half + 8 * nt + 2 * qd;
+          const int t = t0 + 16 * m + g + (e >> 1) * 8, j = 8 * nt + 2 * qd;
           if (t < a.n_tok) {
-            bad |= !isfinite(acc[nt][e]) || !isfinite(acc[nt][e + 1]);
+            bad |= !isfinite(o1[nt][e]) || !isfinite(o1[nt][e + 1]);
             *reinterpret_cast<float2*>(a.o + (size_t)b * a.o_bs + (size_t)t * a.o_ts +
                                        (size_t)h * a.dv + sl * DS + j) =
-                make_float2(acc[nt][e], acc[nt][e + 1]);
+                make_float2(o1[nt][e], o1[nt][e + 1]);
           }
         }
     }
-    __syncthreads();  // S0 is read above; now it is updated
-    // ---- S = gamma_C S0 + W^T diag(exp(L_C - L)) K  (3xTF32) --------------------------------
+    // ---- S = gamma_C S0 + W^T diag(exp(L_C - L)) K  (3xTF32), warp w: its 16 x 64 share -------
     {
       float acc[8][4];
       zero(acc);
-      warp_mma<8, true>(acc, 16 * mt, 64 * half, 0, C,
-                        [&](int m, int k) { return sm.r[k][m] * sm.rdec[k]; },
-                        [&](int k, int n) { return sm.k[k][n]; });
+      warp_mma<8, true, false, false>(acc, &sm.r[0][0], LDR, &sm.k[0][0], LDK, 16 * mt,
+                                      64 * half, 0, C, sm.rdec);
       const float gc = sm.gam[C - 1];
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
