@@ -161,6 +161,20 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
     const int t0 = c * C;
     __syncthreads();  // previous chunk's readers of k, q, r are done
     // ---- loads: K, Q (normalised), V slice (raw), beta, log decay -------------------------
+    // warp 0: this chunk's log decays and betas first (the scan below waits on them)
+    float l0 = 0.f, l1 = 0.f, be0 = 0.f, be1 = 0.f;
+    if (warp == 0) {
+      const int t = t0 + 2 * lane;
+      const size_t gi = ((size_t)b * a.n_tok + t) * a.n_vh + h;
+      if (t < a.n_tok) {
+        l0 = lgs[gi];
+        be0 = gates[gi].x;
+      }
+      if (t + 1 < a.n_tok) {
+        l1 = lgs[gi + a.n_vh];
+        be1 = gates[gi + a.n_vh].x;
+      }
+    }
     {
       // all loads first (one round trip), then the shared-memory stores
       constexpr int NKQ = C * DK / 4 / THREADS, NV = C * DS / 4 / THREADS;
@@ -221,10 +235,6 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
     }
     if (warp == 0) {
       // inclusive scan of the log decays (two tokens per lane); padded tokens: beta 0, decay 1
-      const int t = t0 + 2 * lane;
-      const size_t gi = ((size_t)b * a.n_tok + t) * a.n_vh + h;
-      const float l0 = t < a.n_tok ? lgs[gi] : 0.f;
-      const float l1 = t + 1 < a.n_tok ? lgs[gi + a.n_vh] : 0.f;
       float s = l0 + l1;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -233,8 +243,8 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
       }
       sm.L[2 * lane] = s - l1;
       sm.L[2 * lane + 1] = s;
-      sm.beta[2 * lane] = t < a.n_tok ? gates[gi].x : 0.f;
-      sm.beta[2 * lane + 1] = t + 1 < a.n_tok ? gates[gi + a.n_vh].x : 0.f;
+      sm.beta[2 * lane] = be0;
+      sm.beta[2 * lane + 1] = be1;
       const float LC = __shfl_sync(0xffffffffu, s, 31);
       sm.gam[2 * lane] = expf(s - l1);
       sm.gam[2 * lane + 1] = expf(s);
