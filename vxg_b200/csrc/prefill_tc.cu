@@ -9,8 +9,8 @@
 //                Q8 records of 32 tokens) from the KV pool into a 3-deep raw ring;
 //   warp 1       MMA issuer (one thread) and TMEM owner;
 //   warps 4-7    softmax: thread = query row = TMEM lane; also Q -> TMEM and the epilogue;
-//   warps 8-15   converters: Q8 records -> f16 hi/lo planes (K and V) in 128-byte-swizzled
-//                shared memory, double-buffered separately for K and V.
+//   warps 2, 3, 8, 10, 11, 12, 14, 15   converters: Q8 records -> f16 hi/lo planes (K and V)
+//                in 128-byte-swizzled shared memory, double-buffered separately for K and V.
 // Tensor memory (512 columns): O [0,256) f32, Q [256,384) f16 pairs, S0/S1 [384,512) f32.  The
 // K hi and lo planes are stacked as 64 B-rows, so one MMA per K-step gives both halves of S:
 //   [S_hi | S_lo] = Q [Kh ; Kl]^T                 (kind::f16, M=128, N=64, 16 K-steps)
@@ -91,6 +91,13 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Warp w issues on scheduler w % 4.  The converters sit on warps 2, 3, 8, 10, 11, 12, 14, 15, so
+// the MMA-issuing warp 1 shares its scheduler only with softmax warp 5 (warps 9 and 13 idle).
+__device__ __forceinline__ int conv_index(int warp) {
+  const int v = (int)((0x76f543f2ffff10ffull >> (4 * warp)) & 0xf);
+  return v == 15 ? -1 : v;
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
@@ -236,18 +243,27 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
       const uint32_t id_pv = tc::idesc_f16(128, HD, true);
       bool ok = wait_or_abort(&sm.q_full, 0, sm, status);
       tc::fence_after_sync();
+      // Descriptors are built once; a K-step only adds its byte offset >> 4 to the start-address
+      // field (the stage buffers lie far below the field's 256 KB limit), so issuing an MMA
+      // costs a few instructions: this thread shares its scheduler with busy warps.
+      const uint64_t kd0 = tc::sdesc_sw128(smem_u32(sm.kpl[0]), 16, 1024);
+      const uint64_t kd1 = tc::sdesc_sw128(smem_u32(sm.kpl[1]), 16, 1024);
+      const uint64_t vh0 = tc::sdesc_sw128(smem_u32(sm.vpl[0][0]), KT * 128, 1024);
+      const uint64_t vh1 = tc::sdesc_sw128(smem_u32(sm.vpl[1][0]), KT * 128, 1024);
+      const uint64_t vl0 = tc::sdesc_sw128(smem_u32(sm.vpl[0][1]), KT * 128, 1024);
+      const uint64_t vl1 = tc::sdesc_sw128(smem_u32(sm.vpl[1][1]), KT * 128, 1024);
       auto pv = [&](int i) -> bool {
         const int st = i & 1;
         if (!wait_or_abort(&sm.vf[st], (i >> 1) & 1, sm, status)) return false;
         if (!wait_or_abort(&sm.p_full[st], (i >> 1) & 1, sm, status)) return false;
         tc::fence_after_sync();
         const uint32_t ph = tm + TM_S + 2 * KT * st, pl = ph + 16;
-        const uint32_t vh = smem_u32(sm.vpl[st][0]), vl = smem_u32(sm.vpl[st][1]);
+        const uint64_t vh = st ? vh1 : vh0, vl = st ? vl1 : vl0;
 #pragma unroll
         for (int kk = 0; kk < KT / 16; ++kk) {
-          // V planes as MN-major B: 64-dim column blocks 4 KB apart, 8-key groups 1 KB apart
-          const uint64_t dh = tc::sdesc_sw128(vh + kk * 2048, KT * 128, 1024);
-          const uint64_t dl = tc::sdesc_sw128(vl + kk * 2048, KT * 128, 1024);
+          // V planes as MN-major B: 64-dim column blocks 4 KB apart, 8-key groups 1 KB apart;
+          // K-step kk starts 16 keys (2 KB) further
+          const uint64_t dh = vh + (uint64_t)(kk * 2048 >> 4), dl = vl + (uint64_t)(kk * 2048 >> 4);
           tc::mma_ts(tm + TM_O, ph + kk * 8, dh, id_pv, (i > 0 || kk > 0) ? 1u : 0u);
           tc::mma_ts(tm + TM_O, ph + kk * 8, dl, id_pv, 1u);
           tc::mma_ts(tm + TM_O, pl + kk * 8, dh, id_pv, 1u);
@@ -260,13 +276,12 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
         const int st = j & 1;
         if (!wait_or_abort(&sm.kf[st], (j >> 1) & 1, sm, status)) { ok = false; break; }
         tc::fence_after_sync();
-        const uint32_t k_s = smem_u32(sm.kpl[st]);
+        const uint64_t kd = st ? kd1 : kd0;
         const uint32_t sd = tm + TM_S + 2 * KT * st;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * (2 * KT * 128) + (kk & 3) * 32;
-          tc::mma_ts(sd, tm + TM_Q + kk * 8, tc::sdesc_sw128(k_s + koff, 16, 1024), id_qk,
-                     kk > 0 ? 1u : 0u);
+          const uint32_t koff = (kk >> 2) * (2 * KT * 128) + (kk & 3) * 32;  // compile-time
+          tc::mma_ts(sd, tm + TM_Q + kk * 8, kd + (uint64_t)(koff >> 4), id_qk, kk > 0 ? 1u : 0u);
         }
         tc::mma_commit(&sm.ke[st]);
         tc::mma_commit(&sm.s_full[st]);
@@ -408,13 +423,13 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
       }
       if (bad) atomicOr(status, kStatusNonFinite);
     }
-  } else if (warp >= 8) {
+  } else if (conv_index(warp) >= 0) {
     // ---------------------------------------------------------------- converters
-    // Lane -> (key, 32-dim block): 8 keys x blocks {0,2,4,6} (warps 8-11) or {1,3,5,7}
-    // (warps 12-15).  Record rows are 68 words apart, so 8 keys start in 8 banks = 0 mod 4, and
+    // Lane -> (key, 32-dim block): 8 keys x blocks {0,2,4,6} (converters 0-3) or {1,3,5,7}
+    // (converters 4-7).  Record rows are 68 words apart, so 8 keys start in 8 banks = 0 mod 4, and
     // those four blocks start at word offsets 0, 1, 2, 3 mod 4: the 32 lanes read 32 distinct
     // banks, and the swizzled 16-byte stores of 8 keys cover all banks once per block.
-    const int wc = warp - 8;
+    const int wc = conv_index(warp);
     const int key = 8 * (wc & 3) + (lane & 7);
     const int c = 2 * (lane >> 3) + (wc >> 2);
     for (int j = 0; j < n_tiles; ++j) {
