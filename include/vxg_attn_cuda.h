@@ -151,6 +151,28 @@ VXG_ATTN_API int vxg_attn_cuda_q8_decode(void* ctx, void* kv, uint32_t n_batch, 
                             float scale, uint32_t max_ctx, float* out, int memkind, void* stream,
                             char* err, size_t cap);
 
+/* The decode step of vxg_attn_cuda_q8_decode on host memory, overlapped with its neighbours.
+ * No counterpart in the reference, whose step is synchronous (llm_prefill.rs:311-369 called once
+ * per token).  The call validates like the host-memory form of vxg_attn_cuda_q8_decode, queues
+ * the upload of its inputs on a copy stream, the step's kernels on the context stream and the
+ * download of `out` on a second copy stream, and returns at once with *ticket naming the step.
+ * Consecutive steps alternate between two device staging slots, so the upload of step t+1 and
+ * the download of step t-1 run while the kernels of step t do; queueing step t+2 first waits for
+ * step t to be back on the host.  Inputs are read, and `out` written, asynchronously: keep the
+ * input buffers unchanged and do not read `out` until vxg_attn_cuda_ticket_wait has returned for
+ * the ticket.  Pinned host memory (vxg_attn_cuda_host_alloc) is required for the copies to
+ * overlap. */
+VXG_ATTN_API int vxg_attn_cuda_q8_decode_host_async(void* ctx, void* kv, uint32_t n_batch,
+                            uint32_t n_head, const int32_t* seq_ids, const int32_t* pos,
+                            const float* q, const float* k_new, const float* v_new,
+                            const float* q_gate, float scale, uint32_t max_ctx, float* out,
+                            uint64_t* ticket, char* err, size_t cap);
+/* Waits until the step `ticket` is back on the host and returns its outcome with the codes of
+ * vxg_attn_cuda_sync (VXG_ATTN_OK, VXG_ATTN_WARN_NONFINITE, VXG_ATTN_ERR_INVALID_OPTION for
+ * skipped out-of-range entries, VXG_ATTN_ERR_INTERNAL).  Ticket 0 and tickets already waited for
+ * return VXG_ATTN_OK. */
+VXG_ATTN_API int vxg_attn_cuda_ticket_wait(void* ctx, uint64_t ticket, char* err, size_t cap);
+
 /* The same decode step as vxg_attn_cuda_q8_decode for callers that cannot allocate device
  * memory.  This entry point has no counterpart in the reference.  It is for engines whose device
  * memory belongs to a budgeted pool or to another framework's allocator, and for decode loops

@@ -179,3 +179,60 @@ def test_nonfinite_query_reports_warning(ctx):
     out = pool.decode(np.zeros(1, np.int32), np.array([49], np.int32), q)
     assert pool.last_rc == 1
     assert np.isnan(out[0, 3]).all() and np.isfinite(np.delete(out[0], 3, axis=0)).all()
+
+
+def test_overlapped_host_steps_match_synchronous_steps(ctx):
+    """vxg_attn_cuda_q8_decode_host_async: a run of appended decode steps whose copies overlap
+    the neighbouring steps' kernels gives, step for step, the bytes of the synchronous
+    host-memory call on an identical pool; the appended Q8 blocks are identical too."""
+    rng = np.random.default_rng(77)
+    lens = [500, 3, 1200, 64, 900]
+    H, n_kv, hd, steps = 16, 2, 256, 7
+    cap = max(lens) + steps + 1
+    pool_a, k_host, v_host, _ = make_pool(ctx, rng, lens, n_kv, hd, cap=cap)
+    pool_b = vxg_b200.KvQ8Pool(ctx, len(lens), n_kv, hd, cap)
+    for s, L in enumerate(lens):
+        pool_b.import_blocks(s, 0, k_host[s, :L], v_host[s, :L])
+    B = len(lens)
+    seq = ctx.pinned_empty((B,), np.int32)
+    seq[...] = np.array([3, 0, 4, 2, 1], np.int32)
+    pos = ctx.pinned_empty((steps, B), np.int32)
+    q = ctx.pinned_empty((steps, B, H, hd), np.float32)
+    kn = ctx.pinned_empty((steps, B, n_kv, hd), np.float32)
+    vn = ctx.pinned_empty((steps, B, n_kv, hd), np.float32)
+    gate = ctx.pinned_empty((steps, B, H, hd), np.float32)
+    for i in range(steps):
+        pos[i] = np.array([lens[s] for s in seq], np.int32) + i
+    q[...] = rng.standard_normal(q.shape)
+    kn[...] = rng.standard_normal(kn.shape)
+    vn[...] = rng.standard_normal(vn.shape)
+    gate[...] = rng.standard_normal(gate.shape)
+    outs = [ctx.pinned_empty((B, H, hd), np.float32) for _ in range(steps)]
+    tickets = []
+    for i in range(steps):
+        tickets.append(pool_b.decode_host_async(seq, pos[i], q[i], kn[i], vn[i], q_gate=gate[i],
+                                                out=outs[i], max_ctx=cap))
+    assert tickets == sorted(tickets) and len(set(tickets)) == steps
+    assert [ctx.wait(t) for t in reversed(tickets)] == [0] * steps
+    assert ctx.wait(tickets[0]) == 0  # waited before
+    for i in range(steps):
+        want = pool_a.decode(np.array(seq), np.array(pos[i]), np.array(q[i]), np.array(kn[i]),
+                             np.array(vn[i]), q_gate=np.array(gate[i]), max_ctx=cap)
+        assert np.array_equal(outs[i], want), f"step {i}"
+    for s, L in enumerate(lens):
+        ka, va = pool_a.export_blocks(s, 0, L + steps)
+        kb, vb = pool_b.export_blocks(s, 0, L + steps)
+        assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+    pool_a.close()
+    pool_b.close()
+
+
+def test_overlapped_host_step_rejects_bad_positions(ctx):
+    pool = vxg_b200.KvQ8Pool(ctx, 2, 2, 256, 16)
+    q = np.zeros((1, 16, 256), np.float32)
+    with pytest.raises(vxg_b200.VxgError) as e:
+        pool.decode_host_async(np.array([0], np.int32), np.array([16], np.int32), q)
+    assert e.value.code == -3  # VXG_ATTN_ERR_BUFFER_TOO_SMALL: position beyond the capacity
+    with pytest.raises(vxg_b200.VxgError):
+        ctx.wait(10 ** 9)
+    pool.close()

@@ -105,6 +105,7 @@ class Context:
         self.device_name = self._err.text
         self.sm_count = lib().vxg_attn_cuda_sm_count(self.h)
         self._pinned = []
+        self._inflight = {}  # ticket -> arrays an overlapped step still reads or writes
 
     def close(self):
         if self.h:
@@ -178,6 +179,14 @@ class Context:
 
     def host_free(self, p):
         lib().vxg_attn_cuda_host_free(self.h, p)
+
+    def wait(self, ticket: int) -> int:
+        """Waits for an overlapped host-memory step (KvQ8Pool.decode_host_async) and returns its
+        status code; the step's input arrays are released."""
+        rc = check(lib().vxg_attn_cuda_ticket_wait(self.h, ctypes.c_uint64(ticket), self._err.buf,
+                                                   self._err.cap), self._err)
+        self._inflight.pop(ticket, None)
+        return rc
 
     def pinned_empty(self, shape, dtype):
         """numpy array in pinned host memory, freed when this context is closed."""
@@ -299,6 +308,36 @@ class KvQ8Pool:
             err.buf, err.cap), err)
         self.last_rc = rc
         return out
+
+    def decode_host_async(self, seq_ids, pos, q, k_new=None, v_new=None, q_gate=None,
+                          scale=None, max_ctx: int = 0, out=None) -> int:
+        """decode() on numpy (ideally pinned) arrays, overlapped with the neighbouring steps
+        (vxg_attn_cuda_q8_decode_host_async).  Returns a ticket; `out` is valid after
+        ctx.wait(ticket).  The arrays must not change until then (references are kept)."""
+        a = _Args(q)
+        if a.device:
+            raise TypeError("decode_host_async takes host (numpy) arrays")
+        B = len(seq_ids)
+        n_head = q.size // (B * self.head_dim)
+        qshape = (B, n_head, self.head_dim)
+        kshape = (B, self.n_head_kv, self.head_dim)
+        if scale is None:
+            scale = 1.0 / math.sqrt(self.head_dim)
+        if out is None:
+            out = np.empty(qshape, np.float32)
+        ptrs = [a.ptr(seq_ids, np.int32, (B,), "seq_ids"), a.ptr(pos, np.int32, (B,), "pos"),
+                a.ptr(q, np.float32, qshape, "q"), a.ptr(k_new, np.float32, kshape, "k_new"),
+                a.ptr(v_new, np.float32, kshape, "v_new"),
+                a.ptr(q_gate, np.float32, qshape, "q_gate")]
+        optr = a.ptr(out, np.float32, qshape, "out", writable=True)
+        ticket = ctypes.c_uint64(0)
+        err = ErrBuf()
+        check(lib().vxg_attn_cuda_q8_decode_host_async(
+            self.ctx.h, self.h, B, n_head, *ptrs, ctypes.c_float(scale), max_ctx, optr,
+            ctypes.byref(ticket), err.buf, err.cap), err)
+        if ticket.value:
+            self.ctx._inflight[ticket.value] = (a.keep, out)
+        return ticket.value
 
     def prefill(self, seq_ids, pos, q, k_new, v_new, q_gate=None, scale=None,
                 max_ctx: int = 0, out=None, stream=None):

@@ -11,6 +11,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
+#include <map>
 #include <set>
 #include <string>
 #include <vector>
@@ -84,6 +85,21 @@ struct Ctx {
   DevBuf aux2;                  // DeltaNet scratch (conv output, normalised q/k, gates)
   DevBuf pre;                   // prefill: dequantised f16 cache
   std::set<struct Kv*> pools;   // KV pools created on this context (orphaned on destroy)
+  // Overlapped host-memory decode steps (vxg_attn_cuda_q8_decode_host_async): two staging
+  // slots; uploads and downloads run on their own streams, so the copies of step t+1 and t-1
+  // overlap the kernels of step t on `stream`.
+  struct Slot {
+    DevBuf buf;                    // inputs, output and a status word of one step
+    uint32_t* h_status = nullptr;  // pinned copy of the step's status word
+    cudaEvent_t up = nullptr, done = nullptr, down = nullptr;
+    uint64_t ticket = 0;           // step held by the slot (0: none)
+    bool open = false;             // its outcome has not been collected yet
+  };
+  Slot slot[2];
+  cudaStream_t up_stream = nullptr, down_stream = nullptr;
+  uint64_t next_ticket = 1;
+  struct Outcome { int code; std::string msg; };
+  std::map<uint64_t, Outcome> outcomes;  // collected, not yet waited for
 };
 
 struct Kv {
@@ -137,6 +153,10 @@ int guarded(void* ctx, void* stream, char* err, size_t cap, F&& body) {
       cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
       // A failed call must never leave a copy targeting caller memory (native/cuda.cu:62-65).
       cudaError_t se = st ? cudaStreamSynchronize(st) : cudaSuccess;
+      for (cudaStream_t cs : {c->up_stream, c->down_stream}) {
+        const cudaError_t ce = cs ? cudaStreamSynchronize(cs) : cudaSuccess;
+        if (se == cudaSuccess) se = ce;
+      }
       if (e.code == VXG_ATTN_ERR_INTERNAL || se != cudaSuccess) {
         c->poisoned = true;
         c->poison = e.what();
@@ -164,6 +184,48 @@ int collect_status(Ctx& c, cudaStream_t st) {
                    "a sequence id or position was outside the KV pool; that entry was skipped");
   if (s & vxg::kStatusNonFinite) return VXG_ATTN_WARN_NONFINITE;
   return VXG_ATTN_OK;
+}
+
+// Outcome of a device status word, with the codes collect_status maps it to.
+int status_outcome(uint32_t s, std::string* msg) {
+  if (s & vxg::kStatusTimeout) {
+    *msg = "a device-side bounded wait gave up";
+    return VXG_ATTN_ERR_INTERNAL;
+  }
+  if (s & vxg::kStatusBadIndex) {
+    *msg = "a sequence id or position was outside the KV pool; that entry was skipped";
+    return VXG_ATTN_ERR_INVALID_OPTION;
+  }
+  if (s & vxg::kStatusNonFinite) return VXG_ATTN_WARN_NONFINITE;
+  return VXG_ATTN_OK;
+}
+
+// Streams, events and pinned status words of the overlapped host-memory path (first use).
+void ensure_overlap(Ctx& c) {
+  if (c.down_stream) return;
+  for (auto& sl : c.slot) {
+    for (cudaEvent_t* e : {&sl.up, &sl.done, &sl.down})
+      if (!*e) check(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "cudaEventCreate");
+    if (!sl.h_status) {
+      check(cudaMallocHost(&sl.h_status, sizeof(uint32_t)), "cudaMallocHost status");
+      *sl.h_status = 0;
+    }
+  }
+  if (!c.up_stream)
+    check(cudaStreamCreateWithFlags(&c.up_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  check(cudaStreamCreateWithFlags(&c.down_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+}
+
+// Waits for the step held by `sl` (output and status word back on the host) and files its
+// outcome under its ticket.
+void collect_slot(Ctx& c, Ctx::Slot& sl) {
+  if (!sl.open) return;
+  check(cudaEventSynchronize(sl.down), "cudaEventSynchronize");
+  Ctx::Outcome o;
+  o.code = status_outcome(*sl.h_status, &o.msg);
+  c.outcomes[sl.ticket] = o;
+  sl.open = false;
+  while (c.outcomes.size() > 4096) c.outcomes.erase(c.outcomes.begin());  // never waited for
 }
 
 // Stages host inputs into the context's device staging buffer.
@@ -338,6 +400,16 @@ void vxg_attn_cuda_destroy(void* h) {
   c->aux.release();
   c->aux2.release();
   c->pre.release();
+  if (c->up_stream) cudaStreamSynchronize(c->up_stream);
+  if (c->down_stream) cudaStreamSynchronize(c->down_stream);
+  for (auto& sl : c->slot) {
+    sl.buf.release();
+    if (sl.h_status) cudaFreeHost(sl.h_status);
+    for (cudaEvent_t e : {sl.up, sl.done, sl.down})
+      if (e) cudaEventDestroy(e);
+  }
+  if (c->up_stream) cudaStreamDestroy(c->up_stream);
+  if (c->down_stream) cudaStreamDestroy(c->down_stream);
   if (c->d_status) cudaFree(c->d_status);
   if (c->h_status) cudaFreeHost(c->h_status);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -677,6 +749,94 @@ int vxg_attn_cuda_q8_decode(void* ctx, void* h, uint32_t n_batch, uint32_t n_hea
           "decode launch");
     sg.download();
     return finish(c, stream, st);
+  });
+}
+
+int vxg_attn_cuda_q8_decode_host_async(void* ctx, void* h, uint32_t n_batch, uint32_t n_head,
+                                       const int32_t* seq_ids, const int32_t* pos,
+                                       const float* q, const float* k_new, const float* v_new,
+                                       const float* q_gate, float scale, uint32_t max_ctx,
+                                       float* out, uint64_t* ticket, char* err, size_t cap) {
+  return guarded(ctx, nullptr, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    Kv& kv = use_q8(c, h);
+    require(ticket != nullptr, VXG_ATTN_ERR_NULL_PTR, "null ticket");
+    *ticket = 0;
+    if (n_batch == 0) return VXG_ATTN_OK;
+    require(seq_ids && pos && q && out, VXG_ATTN_ERR_NULL_PTR, "null input");
+    require((k_new == nullptr) == (v_new == nullptr), VXG_ATTN_ERR_NULL_PTR,
+            "k_new and v_new must both be given or both be NULL");
+    check_decode_shape(kv, n_batch, n_head);
+    check_host_positions(kv, n_batch, seq_ids, pos, 1);
+    ensure_overlap(c);
+    const uint64_t t = c.next_ticket++;
+    Ctx::Slot& sl = c.slot[t & 1];
+    collect_slot(c, sl);  // the step two back is done with this slot's buffers
+    const size_t ib = (size_t)n_batch * sizeof(int32_t);
+    const size_t qb = (size_t)n_batch * n_head * kv.hd * sizeof(float);
+    const size_t kvd = (size_t)n_batch * kv.n_kv * kv.hd * sizeof(float);
+    Carver cv;
+    const size_t o_seq = cv.take(ib), o_pos = cv.take(ib), o_q = cv.take(qb);
+    const size_t o_k = k_new ? cv.take(kvd) : 0, o_v = v_new ? cv.take(kvd) : 0;
+    const size_t o_g = q_gate ? cv.take(qb) : 0, o_out = cv.take(qb);
+    const size_t o_st = cv.take(sizeof(uint32_t));
+    sl.buf.reserve(cv.off, "cudaMalloc overlapped staging");
+    uint8_t* base = static_cast<uint8_t*>(sl.buf.p);
+    auto up = [&](size_t off, const void* src, size_t bytes) -> const void* {
+      if (!src) return nullptr;
+      check(cudaMemcpyAsync(base + off, src, bytes, cudaMemcpyHostToDevice, c.up_stream),
+            "upload");
+      return base + off;
+    };
+    const int32_t* dseq = static_cast<const int32_t*>(up(o_seq, seq_ids, ib));
+    const int32_t* dpos = static_cast<const int32_t*>(up(o_pos, pos, ib));
+    const float* dq = static_cast<const float*>(up(o_q, q, qb));
+    const float* dk = static_cast<const float*>(up(o_k, k_new, kvd));
+    const float* dv = static_cast<const float*>(up(o_v, v_new, kvd));
+    const float* dg = static_cast<const float*>(up(o_g, q_gate, qb));
+    float* dout = reinterpret_cast<float*>(base + o_out);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(base + o_st);
+    check(cudaEventRecord(sl.up, c.up_stream), "cudaEventRecord");
+    check(cudaStreamWaitEvent(c.stream, sl.up, 0), "cudaStreamWaitEvent");
+    check(cudaMemsetAsync(dst, 0, sizeof(uint32_t), c.stream), "status reset");
+    if (dk)
+      check(vxg::launch_q8_append(dseq, dpos, dk, dv, kv.k, kv.v, (int)n_batch, 1, (int)kv.n_seq,
+                                  (int)kv.cap, (int)kv.n_kv, (int)(kv.hd / 32), dst, c.stream),
+            "q8_append launch");
+    vxg::DecodeArgs a = decode_args(kv, n_batch, n_head, dseq, nullptr, dpos, 1, dq, scale,
+                                    max_ctx, dst);
+    vxg::Partials p = carve_partials(c, a);
+    cudaEvent_t e0, e1;
+    record_timing(c, &e0, &e1);
+    check(vxg::launch_decode(a, p, dg, dout, c.sm_count, c.force_generic, c.stream, e0, e1),
+          "decode launch");
+    check(cudaEventRecord(sl.done, c.stream), "cudaEventRecord");
+    check(cudaStreamWaitEvent(c.down_stream, sl.done, 0), "cudaStreamWaitEvent");
+    check(cudaMemcpyAsync(out, dout, qb, cudaMemcpyDeviceToHost, c.down_stream), "download");
+    check(cudaMemcpyAsync(sl.h_status, dst, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                          c.down_stream),
+          "status download");
+    check(cudaEventRecord(sl.down, c.down_stream), "cudaEventRecord");
+    sl.ticket = t;
+    sl.open = true;
+    *ticket = t;
+    return VXG_ATTN_OK;
+  });
+}
+
+int vxg_attn_cuda_ticket_wait(void* ctx, uint64_t ticket, char* err, size_t cap) {
+  return guarded(ctx, nullptr, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    if (ticket == 0) return VXG_ATTN_OK;
+    require(ticket < c.next_ticket, VXG_ATTN_ERR_INVALID_OPTION, "unknown ticket");
+    for (auto& sl : c.slot)
+      if (sl.open && sl.ticket == ticket) collect_slot(c, sl);
+    auto it = c.outcomes.find(ticket);
+    if (it == c.outcomes.end()) return VXG_ATTN_OK;  // waited for before
+    const Ctx::Outcome o = it->second;
+    c.outcomes.erase(it);
+    if (o.code < 0) throw AbiError(o.code, o.msg);
+    return o.code;
   });
 }
 
