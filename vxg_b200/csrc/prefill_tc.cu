@@ -48,9 +48,12 @@ struct __align__(1024) Smem {
   uint8_t vpl[2][2][PLANE];       // [stage][hi/lo]: [dim/64 (4)][key (32)][128 B]
   uint8_t raw[NRAW][2][KT * REC]; // [stage][K/V][key][272 B]
   uint64_t raw_full[NRAW], raw_empty[NRAW];
-  uint64_t kf[2], ke[2], vf[2], ve[2];
-  uint64_t s_full[2], p_full[2];
-  uint64_t o_done[2];             // PV of tile i completes phase i >> 1 of o_done[i & 1]
+  uint64_t kf[2], vf[2];          // K / V planes of stage s written (converters -> issuer)
+  uint64_t p_full[2];             // P of tile i written (softmax -> issuer)
+  // QK / PV of tile i complete phase i >> 1 of qk_done / pv_done[i & 1]: one commit each tells
+  // the softmax that S (resp. O) is ready and the converters that the K (resp. V) planes of
+  // stage i & 1 are free
+  uint64_t qk_done[2], pv_done[2];
   uint64_t q_full, drain;
   uint32_t tmem;
   volatile int abort;
@@ -198,13 +201,10 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.kf[i], 8);
       mbar_init(&sm.vf[i], 8);
-      mbar_init(&sm.ke[i], 1);
-      mbar_init(&sm.ve[i], 1);
-      mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.qk_done[i], 1);
+      mbar_init(&sm.pv_done[i], 1);
       mbar_init(&sm.p_full[i], ROWS);
     }
-    mbar_init(&sm.o_done[0], 1);
-    mbar_init(&sm.o_done[1], 1);
     mbar_init(&sm.q_full, ROWS);
     mbar_init(&sm.drain, 1);
     sm.abort = 0;
@@ -268,8 +268,7 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
           tc::mma_ts(tm + TM_O, ph + kk * 8, dl, id_pv, 1u);
           tc::mma_ts(tm + TM_O, pl + kk * 8, dh, id_pv, 1u);
         }
-        tc::mma_commit(&sm.ve[st]);
-        tc::mma_commit(&sm.o_done[st]);
+        tc::mma_commit(&sm.pv_done[st]);
         return true;
       };
       for (int j = 0; ok && j < n_tiles; ++j) {
@@ -283,8 +282,7 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
           const uint32_t koff = (kk >> 2) * (2 * KT * 128) + (kk & 3) * 32;  // compile-time
           tc::mma_ts(sd, tm + TM_Q + kk * 8, kd + (uint64_t)(koff >> 4), id_qk, kk > 0 ? 1u : 0u);
         }
-        tc::mma_commit(&sm.ke[st]);
-        tc::mma_commit(&sm.s_full[st]);
+        tc::mma_commit(&sm.qk_done[st]);
         if (j > 0 && !pv(j - 1)) { ok = false; break; }
       }
       if (ok && n_tiles > 0) pv(n_tiles - 1);
@@ -327,14 +325,14 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
     const float sl2 = a.scale * 1.4426950408889634f;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    // PV of tile i done.  A waiter never lags two phases of o_done[i & 1] behind: PV of tile
+    // PV of tile i done.  A waiter never lags two phases of pv_done[i & 1] behind: PV of tile
     // i + 2 needs this thread's P of tile i + 2 first.
     auto wait_pv = [&](int i) -> bool {
-      return wait_or_abort(&sm.o_done[i & 1], (i >> 1) & 1, sm, status);
+      return wait_or_abort(&sm.pv_done[i & 1], (i >> 1) & 1, sm, status);
     };
     for (int j = 0; j < n_tiles; ++j) {
       const int st = j & 1;
-      if (!wait_or_abort(&sm.s_full[st], (j >> 1) & 1, sm, status)) { ok = false; break; }
+      if (!wait_or_abort(&sm.qk_done[st], (j >> 1) & 1, sm, status)) { ok = false; break; }
       __syncwarp();
       tc::fence_after_sync();
       uint32_t sv[32], sl[32];
@@ -437,14 +435,14 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
       if (!wait_or_abort(&sm.raw_full[rs], (j / NRAW) & 1, sm, status)) break;
       const bool valid = j * KT + key < key_end;
       // K planes of stage st are free once QK of tile j-2 is done
-      if (j >= 2 && !wait_or_abort(&sm.ke[st], ((j >> 1) - 1) & 1, sm, status)) break;
+      if (j >= 2 && !wait_or_abort(&sm.qk_done[st], ((j >> 1) - 1) & 1, sm, status)) break;
       pftc::convert_block(sm.raw[rs][0] + key * REC + c * kBlk, sm.kpl[st],
                           sm.kpl[st] + KT * 128, 2 * KT * 128, key, c, valid);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.kf[st]);
       // V planes of stage st are free once PV of tile j-2 is done
-      if (j >= 2 && !wait_or_abort(&sm.ve[st], ((j >> 1) - 1) & 1, sm, status)) break;
+      if (j >= 2 && !wait_or_abort(&sm.pv_done[st], ((j >> 1) - 1) & 1, sm, status)) break;
       pftc::convert_block(sm.raw[rs][1] + key * REC + c * kBlk, sm.vpl[st][0], sm.vpl[st][1],
                           KT * 128, key, c, valid);
       fence_proxy_async_smem();
