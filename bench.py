@@ -303,6 +303,100 @@ def cpu_baseline_decode(pool, lens, n, budget_s=12.0, n_sample=8):
                       f"append+attend step each, x{reps} repetitions, {el:.1f} s"}
 
 
+def _timed_reps(fn, budget_s, max_reps=1000):
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= max_reps:
+            return reps, el
+
+
+def cpu_baseline_long(pool, L, q, kn, vn, budget_s=10.0):
+    """Config 3 on the oracle port: append + attend of the 262144-token sequence (its real cache,
+    exported from the device), one thread as in the reference's per-sequence step."""
+    from oracle import oracle
+    from vxg_b200 import workloads as wl
+    k, v = pool.export_blocks(0, 0, L)
+    cap = L + 1
+    kp = np.zeros((1, cap, wl.HKV, wl.HD // 32, 34), np.uint8)
+    vp = np.zeros_like(kp)
+    kp[0, :L], vp[0, :L] = k, v
+    kf, vf = kp.reshape(-1), vp.reshape(-1)
+    seq, pos = np.zeros(1, np.int32), np.array([L], np.int32)
+    qh, kh, vh = (x.reshape(1, -1, wl.HD) for x in (q, kn, vn))
+    reps, el = _timed_reps(lambda: oracle.batch_decode_q8(seq, pos, qh, kh, vh, kf, vf, cap,
+                                                           wl.HQ, wl.HKV, wl.HD, do_append=True,
+                                                           n_threads=1), budget_s)
+    return {"value": reps / el, "unit": "seq-steps/s", "cores": 1, "kind": "port",
+            "sample": f"the full step (ctx {L}), x{reps} repetitions, {el:.1f} s"}
+
+
+def cpu_baseline_deltanet(q, k, v, br, ar, A, dt, state, budget_s=10.0):
+    """Config 4 on the oracle port: the batched core step over all 64 sequences x 32 heads (the
+    bench's own state and inputs), sequences spread over the host's cores."""
+    from oracle import oracle
+    B, H, D, _ = state.shape
+    cores = host_cores()
+    st = np.ascontiguousarray(state, dtype=np.float32)
+    reps, el = _timed_reps(lambda: oracle.batch_deltanet(q, k, v, br, ar, A, dt, H, H, D, D, 1e-6,
+                                                         1.0 / np.sqrt(D), st, n_threads=cores),
+                           budget_s)
+    return {"value": B * reps / el, "unit": "seq-steps/s", "cores": cores, "kind": "port",
+            "sample": f"all {B} sequences x {H} heads per step, x{reps} steps, {el:.1f} s"}
+
+
+def cpu_baseline_prefill(pool, q, B, N, H, KV, HD, budget_s=12.0, per_prompt=16):
+    """Config 5a on the oracle port: the reference runs prompt token t as one decode step over
+    the cache [0, t] (llm_prefill.rs:497-517).  Sample: per prompt, `per_prompt` tokens at
+    evenly spaced positions (their mean cost is the prompt's mean cost), attending over the real
+    Q8 cache the GPU prefill wrote; all host cores over the sampled tokens."""
+    from oracle import oracle
+    cores = host_cores()
+    kp = np.zeros((B, N, KV, HD // 32, 34), np.uint8)
+    vp = np.zeros_like(kp)
+    for b in range(B):
+        kp[b], vp[b] = pool.export_blocks(b, 0, N)
+    kf, vf = kp.reshape(-1), vp.reshape(-1)
+    t_idx = ((np.arange(per_prompt) + 0.5) * N / per_prompt).astype(np.int64)
+    seq = np.repeat(np.arange(B, dtype=np.int32), per_prompt)
+    pos = np.tile(t_idx, B).astype(np.int32)
+    import torch
+    qs = q[:, torch.as_tensor(t_idx, device=q.device)].float().cpu().numpy()
+    qs = qs.reshape(B * per_prompt, H, HD)
+    reps, el = _timed_reps(lambda: oracle.batch_decode_q8(seq, pos, qs, None, None, kf, vf, N, H,
+                                                           KV, HD, do_append=False,
+                                                           n_threads=cores), budget_s)
+    n = B * per_prompt
+    return {"value": n * reps / el, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{per_prompt} evenly spaced tokens of each of {B} prompts, attend over "
+                      f"their prefix, x{reps} repetitions, {el:.1f} s"}
+
+
+def cpu_baseline_dnet_prefill(q, k, v, br, ar, A, dt, state0, budget_s=10.0, n_tok=64):
+    """Config 5b on the oracle port: the reference's token-by-token recurrence
+    (llm_prefill.rs:470-480) over the first `n_tok` tokens of every prompt, all heads, prompts
+    spread over the host's cores."""
+    from oracle import oracle
+    B, H, D, _ = state0.shape
+    cores = host_cores()
+    qh, kh, vh = (x[:, :n_tok].cpu().numpy() for x in (q, k, v))
+    bh, ah = br[:, :n_tok].cpu().numpy(), ar[:, :n_tok].cpu().numpy()
+    An, dtn = A.cpu().numpy(), dt.cpu().numpy()
+
+    def run():
+        st = state0.cpu().numpy().copy()
+        for t in range(n_tok):
+            oracle.batch_deltanet(qh[:, t], kh[:, t], vh[:, t], bh[:, t], ah[:, t], An, dtn, H, H,
+                                  D, D, 1e-6, 1.0 / np.sqrt(D), st, n_threads=cores)
+
+    reps, el = _timed_reps(run, budget_s)
+    return {"value": B * n_tok * reps / el, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"the first {n_tok} tokens of each of {B} prompts, all {H} heads, "
+                      f"x{reps} repetitions, {el:.1f} s"}
+
+
 def run_deltanet(args, world, rank, local):
     """64 seqs x 32 heads, dk = dv = 128, state R+W per step."""
     import torch
@@ -341,7 +435,7 @@ def run_deltanet(args, world, rank, local):
     alg = 2 * B * H * D * D * 4 + B * H * 4 * D * 4
     peak, peak_kind = measured_peaks()
     ach = alg / (ms / K * 1e-3) / 1e9
-    return {
+    res = {
         "metric": "gated-DeltaNet decode step: HBM GB/s and seq-steps/s",
         "value": B * world * K / (ms * 1e-3), "unit": "seq-steps/s", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
@@ -354,6 +448,12 @@ def run_deltanet(args, world, rank, local):
                      "traffic": profile_traffic("deltanet_step_config4.json")},
         "gpu_launches": K, "clocks": sampler.summary(),
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        i = W
+        res["cpu_baseline"] = cpu_baseline_deltanet(
+            q[i].cpu().numpy(), k[i].cpu().numpy(), v[i].cpu().numpy(), br[i].cpu().numpy(),
+            ar[i].cpu().numpy(), A.cpu().numpy(), dt.cpu().numpy(), state.cpu().numpy())
+    return res
 
 
 def run_long(args, world, rank, local):
@@ -428,7 +528,7 @@ def run_long(args, world, rank, local):
     alg = (L + W + K / 2) * wl.TOKEN_BYTES / world
     peak, peak_kind = measured_peaks()
     ach = alg / (split * 1e-3) / 1e9
-    return {"metric": METRIC, "value": K / (ms * 1e-3), "unit": "seq-steps/s", "n_gpus": world,
+    res = {"metric": METRIC, "value": K / (ms * 1e-3), "unit": "seq-steps/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "config3: B=1 ctx 262144, 1% K rows x8, split-KV over SMs"
@@ -439,6 +539,11 @@ def run_long(args, world, rank, local):
                          "peak": peak, "unit": "GB/s", "frac": ach / peak,
                          "peak_kind": peak_kind, "split_ms_per_launch": split},
             "gpu_launches": (3 if world == 1 else 4) * K, "clocks": sampler.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        i = W + 2 * K - 1
+        res["cpu_baseline"] = cpu_baseline_long(pool, L + W + K, q[i].cpu().numpy(),
+                                                kn[i].cpu().numpy(), vn[i].cpu().numpy())
+    return res
 
 
 def measured_tensor_peak(sustained=False):
@@ -498,12 +603,14 @@ def run_prefill(args, world, rank, local):
         "config": {"workload": f"config5a: {B} prompts x 8192 tokens per GPU, 16 q / 2 kv heads, "
                                "head_dim 256, bf16 N(0,1) q/k/v, K/V appended to the Q8 cache",
                    "l2": "inputs larger than L2 (1.1 GB of q/k/v/out per step)"},
-        "roofline": {"kernel": "prefill_attn_kernel", "bound": "tensor", "achieved": ach,
+        "roofline": {"kernel": "prefill_tc_kernel", "bound": "tensor", "achieved": ach,
                      "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                      "peak_kind": peak_kind + " (sustained bf16)",
                      "flop_per_launch": flop, "attn_ms_per_launch": attn},
         "gpu_launches": 3 * K, "clocks": sampler.summary(),
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_prefill(pool, q, B, N, H, KV, HD)
     pool.close()
     ctx.close()
     return res
@@ -568,6 +675,8 @@ def run_dnet_prefill(args, world, rank, local):
                              "runs on mma.sync TF32 (3xTF32 for the solve and state update)"},
         "gpu_launches": 3 * K, "clocks": sampler.summary(),
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_dnet_prefill(q, k, v, br, ar, A, dt, state0)
     ctx.close()
     return res
 
