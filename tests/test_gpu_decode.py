@@ -236,3 +236,23 @@ def test_overlapped_host_step_rejects_bad_positions(ctx):
     with pytest.raises(vxg_b200.VxgError):
         ctx.wait(10 ** 9)
     pool.close()
+
+
+@pytest.mark.parametrize("with_gate", [True, False])
+def test_wide_batch_single_pass_combine(ctx, with_gate):
+    """Batches of >= 32 entries take the single-pass combine (one CTA per entry and 16-dim
+    chunk): ragged lengths from 1 token to several split segments, repeated sequence ids, with
+    and without the sigmoid gate."""
+    rng = np.random.default_rng(131)
+    lens = [int(x) for x in rng.integers(1, 2500, 40)] + [2, 1, 96, 97, 5000]
+    pool, kh, vh, cap = make_pool(ctx, rng, lens, 2, 256)
+    B = 48
+    seq = np.concatenate([rng.permutation(len(lens)), rng.integers(0, len(lens), B - len(lens))])
+    seq = seq.astype(np.int32)
+    pos = np.array([lens[s] - 1 for s in seq], np.int32)
+    q = rng.standard_normal((B, 16, 256)).astype(np.float32)
+    gate = rng.standard_normal((B, 16, 256)).astype(np.float32) if with_gate else None
+    out = pool.decode(seq, pos, q, q_gate=gate, max_ctx=cap)
+    want = oracle_decode(kh, vh, cap, seq, pos, q, 2, 256, gates=gate)
+    np.testing.assert_allclose(out, want, atol=ATOL, rtol=RTOL)
+    pool.close()
