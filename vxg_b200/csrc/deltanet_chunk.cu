@@ -30,10 +30,10 @@ constexpr int LDR = DS + 4;       // R: V rows -> right-hand side -> W
 constexpr int LDA = C + 8;        // A / T, P
 
 struct __align__(16) Smem {
-  float k[C][LDK];
-  float q[C][LDK];
+  float k[2][C][LDK];  // chunk c in k[c & 1]; chunk c + 1 lands in the other while c computes
+  float q[C][LDK];     // refilled with chunk c + 1 once chunk c's last Q product is done
   float s[DS][LDK];
-  float r[C][LDR];
+  float r[2][C][LDR];  // V rows -> right-hand side -> W; double-buffered like k
   float a[C][LDA];   // A, then T's diagonal blocks in place
   float p[C][LDA];   // M o Q K^T
   float L[C];        // cumulative log decay
@@ -54,6 +54,20 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
 __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
   hi = __float_as_uint(x) & 0xFFFFE000u;
   lo = __float_as_uint(x - __uint_as_float(hi));
+}
+
+// 16-byte asynchronous global -> shared copy (zero fill when !valid; src must stay a valid
+// address), committed as one group per call site and awaited with cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)),
+               "l"(gmem), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // acc[nt] (+)= A(m0.., k) B(k, n0 + 8 nt ..) over k in [k0, k1): one 16-row tile, NT 8-col
@@ -157,82 +171,68 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
   const int n_chunks = (a.n_tok + C - 1) / C;
   const int mt = warp >> 1, half = warp & 1;  // 64 x 64 outputs: m-tile, 4 of the 8 n-tiles
 
+  // ---- asynchronous chunk loads: K, Q (normalised) and this CTA's V slice ---------------------
+  constexpr int NKQ = C * DK / 4 / THREADS, NV = C * DS / 4 / THREADS;
+  auto issue_kv = [&](int cc) {  // chunk cc's K rows -> k[cc & 1], V rows -> r[cc & 1]
+#pragma unroll
+    for (int u = 0; u < NKQ; ++u) {
+      const int i = tid + u * THREADS, r = i / (DK / 4), c4 = (i % (DK / 4)) * 4;
+      const int t = cc * C + r;
+      const bool ok = t < a.n_tok;
+      cp_async16(&sm.k[cc & 1][r][c4],
+                 kn + (((size_t)b * a.n_tok + (ok ? t : 0)) * a.n_kh + hk) * DK + c4, ok);
+    }
+#pragma unroll
+    for (int u = 0; u < NV; ++u) {
+      const int i = tid + u * THREADS, r = i / (DS / 4), j4 = (i % (DS / 4)) * 4;
+      const int t = cc * C + r;
+      const bool ok = t < a.n_tok;
+      cp_async16(&sm.r[cc & 1][r][j4],
+                 a.v + (size_t)b * a.v_bs + (size_t)(ok ? t : 0) * a.v_ts + (size_t)h * a.dv +
+                     sl * DS + j4,
+                 ok);
+    }
+    cp_async_commit();
+  };
+  auto issue_q = [&](int cc) {  // chunk cc's Q rows -> q
+#pragma unroll
+    for (int u = 0; u < NKQ; ++u) {
+      const int i = tid + u * THREADS, r = i / (DK / 4), c4 = (i % (DK / 4)) * 4;
+      const int t = cc * C + r;
+      const bool ok = t < a.n_tok;
+      cp_async16(&sm.q[r][c4],
+                 qn + (((size_t)b * a.n_tok + (ok ? t : 0)) * a.n_kh + hk) * DK + c4, ok);
+    }
+    cp_async_commit();
+  };
+  // warp 0 keeps the next chunk's log decays and betas in registers (two tokens per lane)
+  float nl0 = 0.f, nl1 = 0.f, nbe0 = 0.f, nbe1 = 0.f;
+  auto load_gates = [&](int cc) {
+    const int t = cc * C + 2 * lane;
+    const size_t gi = ((size_t)b * a.n_tok + t) * a.n_vh + h;
+    nl0 = nl1 = nbe0 = nbe1 = 0.f;
+    if (t < a.n_tok) {
+      nl0 = lgs[gi];
+      nbe0 = gates[gi].x;
+    }
+    if (t + 1 < a.n_tok) {
+      nl1 = lgs[gi + a.n_vh];
+      nbe1 = gates[gi + a.n_vh].x;
+    }
+  };
+  issue_kv(0);
+  issue_q(0);
+  if (warp == 0) load_gates(0);
+
   for (int c = 0; c < n_chunks; ++c) {
     const int t0 = c * C;
-    __syncthreads();  // previous chunk's readers of k, q, r are done
-    // ---- loads: K, Q (normalised), V slice (raw), beta, log decay -------------------------
-    // warp 0: this chunk's log decays and betas first (the scan below waits on them)
-    float l0 = 0.f, l1 = 0.f, be0 = 0.f, be1 = 0.f;
-    if (warp == 0) {
-      const int t = t0 + 2 * lane;
-      const size_t gi = ((size_t)b * a.n_tok + t) * a.n_vh + h;
-      if (t < a.n_tok) {
-        l0 = lgs[gi];
-        be0 = gates[gi].x;
-      }
-      if (t + 1 < a.n_tok) {
-        l1 = lgs[gi + a.n_vh];
-        be1 = gates[gi + a.n_vh].x;
-      }
-    }
-    {
-      // all loads first (one round trip), then the shared-memory stores
-      constexpr int NKQ = C * DK / 4 / THREADS, NV = C * DS / 4 / THREADS;
-      float4 kv[NKQ], qv[NKQ], vv[NV];
-#pragma unroll
-      for (int u = 0; u < NKQ; ++u) {
-        const int i = tid + u * THREADS, r = i / (DK / 4), c4 = (i % (DK / 4)) * 4;
-        const int t = t0 + r;
-        kv[u] = qv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < a.n_tok) {
-          const size_t off = (((size_t)b * a.n_tok + t) * a.n_kh + hk) * DK + c4;
-          kv[u] = *reinterpret_cast<const float4*>(kn + off);
-          qv[u] = *reinterpret_cast<const float4*>(qn + off);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < NV; ++u) {
-        const int i = tid + u * THREADS, r = i / (DS / 4), j4 = (i % (DS / 4)) * 4;
-        const int t = t0 + r;
-        vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < a.n_tok)
-          vv[u] = *reinterpret_cast<const float4*>(a.v + (size_t)b * a.v_bs +
-                                                   (size_t)t * a.v_ts + (size_t)h * a.dv +
-                                                   sl * DS + j4);
-      }
-#pragma unroll
-      for (int u = 0; u < NKQ; ++u) {
-        const int i = tid + u * THREADS, r = i / (DK / 4), c4 = (i % (DK / 4)) * 4;
-        *reinterpret_cast<float4*>(&sm.k[r][c4]) = kv[u];
-        *reinterpret_cast<float4*>(&sm.q[r][c4]) = qv[u];
-      }
-#pragma unroll
-      for (int u = 0; u < NV; ++u) {
-        const int i = tid + u * THREADS, r = i / (DS / 4), j4 = (i % (DS / 4)) * 4;
-        *reinterpret_cast<float4*>(&sm.r[r][j4]) = vv[u];
-      }
-    }
-    // the next chunk's rows go to L2 while this one computes
-    if (c + 1 < n_chunks) {
-      const int tn = t0 + C + (tid & 63);
-      if (tn < a.n_tok) {
-        const int part = tid >> 6;  // 4 threads per token row: K, Q halves, V, gates
-        const size_t off = (((size_t)b * a.n_tok + tn) * a.n_kh + hk) * DK;
-        const float* vrow = a.v + (size_t)b * a.v_bs + (size_t)tn * a.v_ts + (size_t)h * a.dv +
-                            sl * DS;
-        const size_t gi = ((size_t)b * a.n_tok + tn) * a.n_vh + h;
-        const void* p0 = part == 0 ? (const void*)(kn + off) : part == 1 ? (const void*)(qn + off)
-                       : part == 2 ? (const void*)vrow : (const void*)(lgs + gi);
-        const void* p1 = part == 0 ? (const void*)(kn + off + 64) : part == 1 ? (const void*)(qn + off + 64)
-                       : part == 2 ? (const void*)(vrow + 32) : (const void*)(gates + gi);
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(p0));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(p1));
-        if (part < 2) {
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const float*>(p0) + 32));
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const float*>(p1) + 32));
-        }
-      }
-    }
+    float(*kb)[LDK] = sm.k[c & 1];
+    float(*rb)[LDR] = sm.r[c & 1];
+    cp_async_wait_all();
+    __syncthreads();  // chunk c's K, Q, V landed; chunk c - 1's readers of k, r are done
+    if (c + 1 < n_chunks) issue_kv(c + 1);
+    const float l0 = nl0, l1 = nl1, be0 = nbe0, be1 = nbe1;
+    if (warp == 0 && c + 1 < n_chunks) load_gates(c + 1);
     if (warp == 0) {
       // inclusive scan of the log decays (two tokens per lane); padded tokens: beta 0, decay 1
       float s = l0 + l1;
@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
     {
       float acc[4][4];
       zero(acc);
-      warp_mma<4, false, true, true>(acc, &sm.k[0][0], LDK, &sm.k[0][0], LDK, 16 * mt,
+      warp_mma<4, false, true, true>(acc, &kb[0][0], LDK, &kb[0][0], LDK, 16 * mt,
                                      32 * half, 0, DK);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
@@ -266,14 +266,14 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
           sm.a[t][i] = i < t ? sm.beta[t] * expf(sm.L[t] - sm.L[i]) * acc[nt][e] : 0.f;
         }
       zero(acc);
-      warp_mma<4, false, true, true>(acc, &sm.k[0][0], LDK, &sm.s[0][0], LDK, 16 * mt,
+      warp_mma<4, false, true, true>(acc, &kb[0][0], LDK, &sm.s[0][0], LDK, 16 * mt,
                                      32 * half, 0, DK);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int t = 16 * mt + g + (e >> 1) * 8, j = 32 * half + 8 * nt + 2 * qd + (e & 1);
-          sm.r[t][j] = sm.beta[t] * (sm.r[t][j] - sm.gam[t] * acc[nt][e]);
+          rb[t][j] = sm.beta[t] * (rb[t][j] - sm.gam[t] * acc[nt][e]);
         }
     }
     __syncthreads();
@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
       const int m = warp - 4;
       float acc[8][4];
       zero(acc);
-      warp_mma<8, false, true, true>(acc, &sm.q[0][0], LDK, &sm.k[0][0], LDK, 16 * m, 0, 0, DK);
+      warp_mma<8, false, true, true>(acc, &sm.q[0][0], LDK, &kb[0][0], LDK, 16 * m, 0, 0, DK);
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
@@ -318,18 +318,18 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
         float acc[2][4];
         zero(acc);
         if (bi > 0)
-          warp_mma<2, true, true, false>(acc, &sm.a[0][0], LDA, &sm.r[0][0], LDR, 16 * bi, n0,
+          warp_mma<2, true, true, false>(acc, &sm.a[0][0], LDA, &rb[0][0], LDR, 16 * bi, n0,
                                          0, 16 * bi);
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int t = 16 * bi + g + (e >> 1) * 8, n = n0 + 8 * nt + 2 * qd + (e & 1);
-            sm.r[t][n] -= acc[nt][e];
+            rb[t][n] -= acc[nt][e];
           }
         __syncwarp();
         zero(acc);
-        warp_mma<2, true, true, false>(acc, &sm.a[0][0], LDA, &sm.r[0][0], LDR, 16 * bi, n0,
+        warp_mma<2, true, true, false>(acc, &sm.a[0][0], LDA, &rb[0][0], LDR, 16 * bi, n0,
                                        16 * bi, 16 * bi + 16);
         __syncwarp();
 #pragma unroll
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int t = 16 * bi + g + (e >> 1) * 8, n = n0 + 8 * nt + 2 * qd + (e & 1);
-            sm.r[t][n] = acc[nt][e];
+            rb[t][n] = acc[nt][e];
           }
         __syncwarp();
       }
@@ -350,11 +350,12 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) o1[nt][e] *= sm.gam[16 * m + g + (e >> 1) * 8];
     }
-    __syncthreads();  // W complete; S0 no longer read
+    __syncthreads();  // W complete; S0 and Q no longer read
+    if (c + 1 < n_chunks) issue_q(c + 1);
     if (warp >= 4) {
       // ---- O = diag(gamma) Q S0^T + P W -> global -------------------------------------------
       const int m = warp - 4;
-      warp_mma<8, false, true, false>(o1, &sm.p[0][0], LDA, &sm.r[0][0], LDR, 16 * m, 0, 0,
+      warp_mma<8, false, true, false>(o1, &sm.p[0][0], LDA, &rb[0][0], LDR, 16 * m, 0, 0,
                                       16 * m + 16);
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
@@ -373,7 +374,7 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
     {
       float acc[8][4];
       zero(acc);
-      warp_mma<8, true, false, false>(acc, &sm.r[0][0], LDR, &sm.k[0][0], LDK, 16 * mt,
+      warp_mma<8, true, false, false>(acc, &rb[0][0], LDR, &kb[0][0], LDK, 16 * mt,
                                       64 * half, 0, C, sm.rdec);
       const float gc = sm.gam[C - 1];
 #pragma unroll
