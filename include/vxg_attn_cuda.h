@@ -25,6 +25,9 @@
  * and returns when the results are in place.  A non-NULL stream (cudaStream_t) makes
  * device-memory calls asynchronous on that stream; call vxg_attn_cuda_sync to collect device
  * status.  One context per host thread; contexts are not thread-safe.
+ * Float / bf16 arrays in device memory (and the KV pools passed to
+ * vxg_attn_cuda_q8_decode_noalloc) must be 16-byte aligned; a misaligned one is rejected with
+ * VXG_ATTN_ERR_INVALID_OPTION.  Host-memory calls accept any alignment.
  */
 #ifndef VXG_ATTN_CUDA_H
 #define VXG_ATTN_CUDA_H

@@ -256,3 +256,20 @@ def test_wide_batch_single_pass_combine(ctx, with_gate):
     want = oracle_decode(kh, vh, cap, seq, pos, q, 2, 256, gates=gate)
     np.testing.assert_allclose(out, want, atol=ATOL, rtol=RTOL)
     pool.close()
+
+
+def test_misaligned_device_arrays_are_rejected(ctx):
+    """Device arrays are accessed with 16-byte vectors and bulk copies: a view that starts one
+    float into an allocation is refused on the host, before any launch."""
+    import torch
+    pool = vxg_b200.KvQ8Pool(ctx, 1, 2, 256, 16)
+    seq = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+    qbuf = torch.zeros(16 * 256 + 1, device="cuda")
+    q = qbuf[1:].view(1, 16, 256)
+    with pytest.raises(vxg_b200.VxgError) as e:
+        pool.decode(seq, pos, q)
+    assert e.value.code == -2 and "aligned" in str(e.value)
+    ok = pool.decode(seq, pos, qbuf[:-1].view(1, 16, 256))
+    assert ctx.sync() == 0 and torch.isfinite(ok).all()
+    pool.close()

@@ -11,6 +11,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
+#include <initializer_list>
 #include <map>
 #include <set>
 #include <string>
@@ -353,6 +354,18 @@ void check_host_positions(const Kv& kv, uint32_t n_batch, const int32_t* seq_ids
   }
 }
 
+// Device arrays are read and written with 8- and 16-byte vector accesses and bulk copies, so
+// device-memory calls take them 16-byte aligned (cudaMalloc and torch allocations are 256-byte
+// aligned; a sub-view stays aligned when it starts at a multiple of 4 floats).  Host-memory
+// calls stage through aligned buffers and take any alignment.
+void require_aligned16(bool host, std::initializer_list<std::pair<const void*, const char*>> arrays) {
+  if (host) return;
+  for (const auto& x : arrays)
+    if (x.first && (reinterpret_cast<uintptr_t>(x.first) & 15u))
+      throw AbiError(VXG_ATTN_ERR_INVALID_OPTION,
+                     std::string(x.second) + " must be 16-byte aligned in device memory");
+}
+
 }  // namespace
 
 // =============================================================================================
@@ -691,6 +704,7 @@ int vxg_attn_cuda_q8_append(void* ctx, void* h, uint32_t n_batch, uint32_t n_tok
     if (n_batch == 0 || n_tok == 0) return VXG_ATTN_OK;
     require(seq_ids && pos && k_new && v_new, VXG_ATTN_ERR_NULL_PTR, "null input");
     const bool host = memkind == VXG_ATTN_MEM_HOST;
+    require_aligned16(host, {{k_new, "k_new"}, {v_new, "v_new"}});
     if (host) check_host_positions(kv, n_batch, seq_ids, pos, n_tok);
     cudaStream_t st = pick_stream(c, stream);
     const size_t kvd = (size_t)n_batch * n_tok * kv.n_kv * kv.hd * sizeof(float);
@@ -722,6 +736,8 @@ int vxg_attn_cuda_q8_decode(void* ctx, void* h, uint32_t n_batch, uint32_t n_hea
             "k_new and v_new must both be given or both be NULL");
     check_decode_shape(kv, n_batch, n_head);
     const bool host = memkind == VXG_ATTN_MEM_HOST;
+    require_aligned16(host, {{q, "q"}, {k_new, "k_new"}, {v_new, "v_new"}, {q_gate, "q_gate"},
+                             {out, "out"}});
     if (host) check_host_positions(kv, n_batch, seq_ids, pos, 1);
     cudaStream_t st = pick_stream(c, stream);
     const size_t qb = (size_t)n_batch * n_head * kv.hd * sizeof(float);
@@ -862,6 +878,8 @@ int vxg_attn_cuda_q8_prefill(void* ctx, void* h, uint32_t n_batch, uint32_t n_to
     const uint32_t lmax = (max_ctx == 0 || max_ctx > kv.cap) ? kv.cap : max_ctx;
     require(n_tok <= lmax, VXG_ATTN_ERR_INVALID_OPTION, "max_ctx below n_tok");
     const bool host = memkind == VXG_ATTN_MEM_HOST;
+    require_aligned16(host, {{q, "q"}, {k_new, "k_new"}, {v_new, "v_new"}, {q_gate, "q_gate"},
+                             {out, "out"}});
     if (host) {
       check_host_positions(kv, n_batch, seq_ids, pos, n_tok);
       for (uint32_t b = 0; b < n_batch; ++b)
@@ -924,6 +942,7 @@ int vxg_attn_cuda_f32_append(void* ctx, void* h, uint32_t n_batch, uint32_t n_to
     if (n_batch == 0 || n_tok == 0) return VXG_ATTN_OK;
     require(seq_ids && pos && k_new && v_new, VXG_ATTN_ERR_NULL_PTR, "null input");
     const bool host = memkind == VXG_ATTN_MEM_HOST;
+    require_aligned16(host, {{k_new, "k_new"}, {v_new, "v_new"}});
     if (host) check_host_positions(kv, n_batch, seq_ids, pos, n_tok);
     cudaStream_t st = pick_stream(c, stream);
     const size_t kvd = (size_t)n_batch * n_tok * kv.n_kv * kv.hd * sizeof(float);
@@ -956,6 +975,8 @@ int vxg_attn_cuda_f32_decode(void* ctx, void* h, uint32_t n_batch, uint32_t n_he
             "k_new and v_new must both be given or both be NULL");
     check_decode_shape(kv, n_batch, n_head);
     const bool host = memkind == VXG_ATTN_MEM_HOST;
+    require_aligned16(host, {{q, "q"}, {k_new, "k_new"}, {v_new, "v_new"}, {q_gate, "q_gate"},
+                             {out, "out"}});
     if (host) check_host_positions(kv, n_batch, seq_ids, pos, 1);
     cudaStream_t st = pick_stream(c, stream);
     const size_t qb = (size_t)n_batch * n_head * kv.hd * sizeof(float);
@@ -999,6 +1020,7 @@ int vxg_attn_cuda_q8_decode_partial(void* ctx, void* h, uint32_t n_batch, uint32
             "null input");
     check_decode_shape(kv, n_batch, n_head);
     const bool host = memkind == VXG_ATTN_MEM_HOST;
+    require_aligned16(host, {{q, "q"}, {m, "m"}, {l, "l"}, {o, "o"}});
     if (host)
       for (uint32_t b = 0; b < n_batch; ++b)
         require(seq_ids[b] >= 0 && (uint32_t)seq_ids[b] < kv.n_seq && kv_begin[b] >= 0 &&
@@ -1037,6 +1059,7 @@ int vxg_attn_cuda_lse_combine(void* ctx, uint32_t n_parts, uint32_t n_rows, uint
     require(n_parts > 0 && head_dim > 0, VXG_ATTN_ERR_INVALID_OPTION, "empty combine");
     cudaStream_t st = pick_stream(c, stream);
     const bool host = memkind == VXG_ATTN_MEM_HOST;
+    require_aligned16(host, {{m, "m"}, {l, "l"}, {o, "o"}, {gate, "gate"}, {out, "out"}});
     const size_t pr = (size_t)n_parts * n_rows;
     Stager sg(c, st, host);
     sg.in(m, pr * sizeof(float));
@@ -1064,6 +1087,7 @@ int vxg_attn_cuda_lse_combine_packed(void* ctx, uint32_t n_parts, uint32_t n_row
     require(n_parts > 0 && head_dim > 0, VXG_ATTN_ERR_INVALID_OPTION, "empty combine");
     cudaStream_t st = pick_stream(c, stream);
     const bool host = memkind == VXG_ATTN_MEM_HOST;
+    require_aligned16(host, {{packed, "packed"}, {gate, "gate"}, {out, "out"}});
     Stager sg(c, st, host);
     sg.in(packed, (size_t)n_parts * n_rows * (head_dim + 2) * sizeof(float));
     sg.in(gate, (size_t)n_rows * head_dim * sizeof(float));
@@ -1255,9 +1279,7 @@ int vxg_attn_cuda_deltanet_step(void* ctx, uint32_t n_batch, uint32_t n_kh, uint
     require(dv > 0 && dv % 32 == 0, VXG_ATTN_ERR_UNSUPPORTED, "dv must be a multiple of 32");
     cudaStream_t st = pick_stream(c, stream);
     const bool host = memkind == VXG_ATTN_MEM_HOST;
-    if (!host)  // the kernel moves q, k and the state in 16-byte vectors
-      require(((uintptr_t)q | (uintptr_t)k | (uintptr_t)state) % 16 == 0,
-              VXG_ATTN_ERR_INVALID_OPTION, "q, k and state must be 16-byte aligned");
+    require_aligned16(host, {{q, "q"}, {k, "k"}, {v, "v"}, {state, "state"}, {o, "o"}});
     Stager sg(c, st, host);
     sg.in(q, (size_t)n_batch * n_kh * dk * sizeof(float));
     sg.in(k, (size_t)n_batch * n_kh * dk * sizeof(float));
@@ -1315,9 +1337,7 @@ int vxg_attn_cuda_deltanet_prefill(void* ctx, uint32_t n_batch, uint32_t n_tok, 
     require(dv > 0 && dv % 32 == 0, VXG_ATTN_ERR_UNSUPPORTED, "dv must be a multiple of 32");
     cudaStream_t st = pick_stream(c, stream);
     const bool host = memkind == VXG_ATTN_MEM_HOST;
-    if (!host)
-      require(((uintptr_t)state % 16) == 0, VXG_ATTN_ERR_INVALID_OPTION,
-              "state must be 16-byte aligned");
+    require_aligned16(host, {{q, "q"}, {k, "k"}, {v, "v"}, {state, "state"}, {o, "o"}});
     const size_t bt = (size_t)n_batch * n_tok;
     Stager sg(c, st, host);
     sg.in(q, bt * n_kh * dk * sizeof(float));
@@ -1386,6 +1406,8 @@ int vxg_attn_cuda_step_deltanet_recurrent(
             "conv_ch must equal 2 * n_kh * dk + n_vh * dv (llm_ops.rs:139-143)");
     cudaStream_t st = pick_stream(c, stream);
     const bool host = memkind == VXG_ATTN_MEM_HOST;
+    require_aligned16(host, {{qkv_mixed, "qkv_mixed"}, {z, "z"}, {conv_state, "conv_state"},
+                             {ssm_state, "ssm_state"}, {y_concat, "y_concat"}});
     if (!host)
       require(((uintptr_t)ssm_state % 16) == 0, VXG_ATTN_ERR_INVALID_OPTION,
               "ssm_state must be 16-byte aligned");

@@ -85,6 +85,13 @@ extern "C" int vxg_attn_cuda_q8_decode_noalloc(
     put(err, cap, "k_new and v_new must both be given or both be NULL");
     return VXG_ATTN_ERR_NULL_PTR;
   }
+  // bulk copies and vector accesses need 16-byte aligned arrays
+  const void* arrays[] = {k_pool, v_pool, q, k_new, v_new, q_gate, out};
+  for (const void* p : arrays)
+    if (p && (reinterpret_cast<uintptr_t>(p) & 15u)) {
+      put(err, cap, "device arrays must be 16-byte aligned");
+      return VXG_ATTN_ERR_INVALID_OPTION;
+    }
   if (head_dim == 0 || head_dim % 32 || head_dim > 256) {
     put(err, cap, "head_dim must be a multiple of 32, at most 256");
     return VXG_ATTN_ERR_UNSUPPORTED;
