@@ -336,6 +336,62 @@ __global__ void __launch_bounds__(128) deltanet_prep_kernel(DeltaNetArgs a, floa
   }
 }
 
+// The same preparation with one warp per (b, t, k head) and 16-byte accesses, for dense q / k
+// rows with 16-byte aligned starts (dk <= 256); the gates take one thread per (b, t, v head).
+__global__ void __launch_bounds__(256) deltanet_prep_vec_kernel(DeltaNetArgs a, float* qn,
+                                                                float* kn, float2* gates,
+                                                                float* lgs) {
+  const int lane = threadIdx.x & 31;
+  const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (w < (long long)a.n_batch * a.n_tok * a.n_kh) {
+    const long long bt = w / a.n_kh;
+    const int hk = (int)(w - bt * a.n_kh);
+    const int b = (int)(bt / a.n_tok), t = (int)(bt - (long long)b * a.n_tok);
+    const float* qg = a.q + (size_t)b * a.q_bs + (size_t)t * a.q_ts + (size_t)hk * a.dk;
+    const float* kg = a.k + (size_t)b * a.k_bs + (size_t)t * a.k_ts + (size_t)hk * a.dk;
+    float4 qv[2], kv[2];
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = 4 * (lane + 32 * u);
+      qv[u] = kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < a.dk) {
+        qv[u] = *reinterpret_cast<const float4*>(qg + i);
+        kv[u] = *reinterpret_cast<const float4*>(kg + i);
+      }
+      sq = fmaf(qv[u].x, qv[u].x, sq); sq = fmaf(qv[u].y, qv[u].y, sq);
+      sq = fmaf(qv[u].z, qv[u].z, sq); sq = fmaf(qv[u].w, qv[u].w, sq);
+      sk = fmaf(kv[u].x, kv[u].x, sk); sk = fmaf(kv[u].y, kv[u].y, sk);
+      sk = fmaf(kv[u].z, kv[u].z, sk); sk = fmaf(kv[u].w, kv[u].w, sk);
+    }
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    const float qs = a.q_scale / sqrtf(sq + a.eps), ks = 1.0f / sqrtf(sk + a.eps);
+    float* qo = qn + ((size_t)bt * a.n_kh + hk) * a.dk;
+    float* ko = kn + ((size_t)bt * a.n_kh + hk) * a.dk;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = 4 * (lane + 32 * u);
+      if (i < a.dk) {
+        *reinterpret_cast<float4*>(qo + i) =
+            make_float4(qv[u].x * qs, qv[u].y * qs, qv[u].z * qs, qv[u].w * qs);
+        *reinterpret_cast<float4*>(ko + i) =
+            make_float4(kv[u].x * ks, kv[u].y * ks, kv[u].z * ks, kv[u].w * ks);
+      }
+    }
+  }
+  const long long gidx = (long long)blockIdx.x * 256 + threadIdx.x;
+  if (gidx < (long long)a.n_batch * a.n_tok * a.n_vh) {
+    const long long bt = gidx / a.n_vh;
+    const int h = (int)(gidx - bt * a.n_vh);
+    const int b = (int)(bt / a.n_tok), t = (int)(bt - (long long)b * a.n_tok);
+    const size_t gi = (size_t)b * a.g_bs + (size_t)t * a.g_ts + h;
+    const float lg = log_decay_of(a.alpha_raw[gi], a.dt_bias[h], a.ssm_a[h]);
+    gates[gidx] = make_float2(sigmoidf_(a.beta_raw[gi]), expf(lg));
+    if (lgs) lgs[gidx] = lg;
+  }
+}
+
 // One CTA = (sequence, v head, chunk of 32 state rows); 8 lanes per row, DK/8 dims per lane.
 // Rows evolve independently in the recurrence, so chunks of rows run in parallel CTAs; each CTA
 // streams the (shared) normalised q, k of every token through L1.
@@ -497,7 +553,17 @@ cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, int al
   float2* gates = reinterpret_cast<float2*>(kn + bt * a.n_kh * a.dk);
   float* lgs = reinterpret_cast<float*>(gates + bt * a.n_vh);
   const bool chunked = allow_chunk && deltanet_chunk_supported(a);
-  deltanet_prep_kernel<<<(unsigned)bt, 128, 0, st>>>(a, qn, kn, gates, chunked ? lgs : nullptr);
+  const bool vec = a.dk % 4 == 0 && a.dk <= 256 && a.q_ts % 4 == 0 && a.q_bs % 4 == 0 &&
+                   a.k_ts % 4 == 0 && a.k_bs % 4 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k)) & 15u) == 0;
+  if (vec) {
+    const long long warps = (long long)bt * a.n_kh, gthreads = (long long)bt * a.n_vh;
+    const long long blocks = std::max((warps + 7) / 8, (gthreads + 255) / 256);
+    deltanet_prep_vec_kernel<<<(unsigned)blocks, 256, 0, st>>>(a, qn, kn, gates,
+                                                              chunked ? lgs : nullptr);
+  } else {
+    deltanet_prep_kernel<<<(unsigned)bt, 128, 0, st>>>(a, qn, kn, gates, chunked ? lgs : nullptr);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (chunked) {
