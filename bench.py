@@ -484,7 +484,8 @@ def run_long(args, world, rank, local):
         step = lambda i: pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=out, max_ctx=cap)
     else:
         from vxg_b200.dist import LongContextDecoder
-        dec = LongContextDecoder(ctx, cap, wl.HQ, wl.HKV, wl.HD, world, rank)
+        dec = LongContextDecoder(ctx, cap, wl.HQ, wl.HKV, wl.HD, world, rank,
+                                 exchange=args.exchange)
         mine = dec.range.local_len(L)
         wl.fill_pool_device(dec.pool, [mine], seed=3 + rank, outlier_frac=0.01)
         step = lambda i: dec.step(L + i, q[i], kn[i], vn[i])
@@ -525,6 +526,8 @@ def run_long(args, world, rank, local):
         split = barrier_max(torch, dist, world, ctx.split_ms_total() / K)
     del graph
     torch.cuda.synchronize()
+    if world > 1:
+        dec.close()
     alg = (L + W + K / 2) * wl.TOKEN_BYTES / world
     peak, peak_kind = measured_peaks()
     ach = alg / (split * 1e-3) / 1e9
@@ -532,8 +535,11 @@ def run_long(args, world, rank, local):
             "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "config3: B=1 ctx 262144, 1% K rows x8, split-KV over SMs"
-                                   + (f" and {world} GPUs (NCCL all-gather + LSE combine, "
-                                      "CUDA graph of the K steps)" if world > 1 else ""),
+                                   + (f" and {world} GPUs ("
+                                      + ("partials through NVLink peer memory, "
+                                         if args.exchange == "peer" else "NCCL all-gather, ")
+                                      + "LSE combine, CUDA graph of the K steps)"
+                                      if world > 1 else ""),
                        "l2": "inputs larger than L2 (285 MB of KV per step)"},
             "roofline": {"kernel": "decode_fast_split", "bound": "hbm", "achieved": ach,
                          "peak": peak, "unit": "GB/s", "frac": ach / peak,
@@ -748,6 +754,8 @@ def main():
     ap.add_argument("--seqs", type=int, default=64, help="sequences per GPU (profiling runs)")
     ap.add_argument("--ctx-max", type=int, default=32768, help="context upper bound (profiling)")
     ap.add_argument("--prompts", type=int, default=8, help="prefill prompts per GPU (profiling)")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="config 3 on N GPUs: partials through NVLink peer memory or NCCL")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -255,6 +255,36 @@ VXG_ATTN_API int vxg_attn_cuda_lse_combine_packed(void* ctx, uint32_t n_parts, u
                                                   const float* gate, float* out, int memkind,
                                                   void* stream, char* err, size_t cap);
 
+/* ---------------------------------------------------------------- NVLink peer exchange ----- */
+/* The all-gather + combine of the long-context KV-range split (vxg_attn_cuda_q8_decode_partial
+ * on every rank, then vxg_attn_cuda_lse_combine_packed over the gathered parts) done through
+ * NVLink peer memory instead of a collective; no counterpart in the reference (its step runs on
+ * one device).  One process per GPU, world <= 8.  Each rank allocates an exchange buffer
+ * (vxg_attn_cuda_peer_alloc, which also returns its 64-byte CUDA IPC handle), hands the handle
+ * to the other ranks by any host channel, and maps theirs with vxg_attn_cuda_peer_open.
+ * vxg_attn_cuda_peer_step then stores this rank's packed partials `send` ([m | l | o], n_rows *
+ * (head_dim + 2) floats) into every rank's buffer and, once every rank's partials of the same
+ * step have arrived (a wait bounded in time; VXG_ATTN_ERR_INTERNAL from vxg_attn_cuda_sync if it
+ * gives up), writes the merged rows to `out` ([n_rows][head_dim], optional sigmoid `gate`).
+ * bufs[r] is rank r's buffer as mapped here (bufs[rank] = the own buffer).  Every rank must
+ * issue the same sequence of steps; the step counter is kept in device memory, so captured CUDA
+ * graphs of steps replay correctly.  Device memory only; asynchronous on `stream` (NULL: the
+ * context stream, synchronous).  Buffers are zero-initialised: allocate all of them before the
+ * first step and free them only after every rank's last step. */
+VXG_ATTN_API size_t vxg_attn_cuda_peer_buffer_bytes(uint32_t world, uint32_t n_rows,
+                                                    uint32_t head_dim);
+VXG_ATTN_API void* vxg_attn_cuda_peer_alloc(void* ctx, uint32_t world, uint32_t n_rows,
+                                            uint32_t head_dim, void* ipc_handle, char* err,
+                                            size_t cap);
+VXG_ATTN_API void* vxg_attn_cuda_peer_open(void* ctx, const void* ipc_handle, char* err,
+                                           size_t cap);
+VXG_ATTN_API void vxg_attn_cuda_peer_close(void* ctx, void* mapped);
+VXG_ATTN_API void vxg_attn_cuda_peer_free(void* ctx, void* buf);
+VXG_ATTN_API int vxg_attn_cuda_peer_step(void* ctx, void* const* bufs, uint32_t world,
+                                         uint32_t rank, uint32_t n_rows, uint32_t head_dim,
+                                         const float* send, const float* gate, float* out,
+                                         void* stream, char* err, size_t cap);
+
 /* Drop-in for step_full_gqa_q8 (llm_prefill.rs:259-278) on host buffers for one sequence `seq`
  * of `kv`: q_raw [n_head][hd] (or [n_head][2*hd] with gated_q), k_cur (updated in place with
  * the normed / RoPE'd K, as in the reference), v_cur [n_head_kv][hd], optional q_norm/k_norm

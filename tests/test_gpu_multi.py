@@ -1,5 +1,6 @@
-"""Two-GPU KV-range split of one long context (NCCL): LongContextDecoder on 2 ranks equals the
-single-GPU decode of the same cache.  Skipped on machines with fewer than 2 GPUs."""
+"""Two-GPU KV-range split of one long context: LongContextDecoder on 2 ranks, with the partials
+exchanged by NCCL or through NVLink peer memory, equals the single-GPU decode of the same cache,
+also when the peer steps are replayed from a CUDA graph.  Skipped with fewer than 2 GPUs."""
 import os
 import socket
 import subprocess
@@ -23,11 +24,11 @@ dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                         device_id=torch.device("cuda", rank))
 rng = np.random.default_rng(5)
 L, cap = 3000, 3100
-k = rng.standard_normal((L + 4, 2, 256)).astype(np.float32)
-v = rng.standard_normal((L + 4, 2, 256)).astype(np.float32)
+k = rng.standard_normal((L + 8, 2, 256)).astype(np.float32)
+v = rng.standard_normal((L + 8, 2, 256)).astype(np.float32)
 kb, vb = oracle.q8_quantize(k), oracle.q8_quantize(v)
 ctx = vxg_b200.Context()
-dec = LongContextDecoder(ctx, cap, 16, 2, 256, world, rank)
+dec = LongContextDecoder(ctx, cap, 16, 2, 256, world, rank, exchange=os.environ["EXCHANGE"])
 lo = dec.range.begin; n = dec.range.local_len(L)
 if n: dec.pool.import_blocks(0, 0, kb[lo:lo + n], vb[lo:lo + n])
 full = vxg_b200.KvQ8Pool(ctx, 1, 2, 256, cap)
@@ -41,13 +42,39 @@ for i in range(4):
                        k_new=k[L + i][None], v_new=v[L + i][None])[0]
     worst = max(worst, float(np.abs(out.cpu().numpy() - want).max()))
 ctx.sync()
+if dec.peer is not None:
+    # the same steps captured once and replayed: the device-side step counter keeps the flags
+    # of both ranks in step across replays
+    qs = [torch.from_numpy(rng.standard_normal((16, 256)).astype(np.float32)).cuda()
+          for _ in range(3)]
+    kn = [torch.from_numpy(k[L + 4 + i]).cuda() for i in range(3)]
+    vn = [torch.from_numpy(v[L + 4 + i]).cuda() for i in range(3)]
+    outs = [torch.empty((16, 256), device="cuda") for _ in range(3)]
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(3):
+            # appends go to fixed positions: replaying rewrites the same tokens
+            outs[i].copy_(dec.step(L + 4 + i, qs[i], kn[i], vn[i]))
+    for rep in range(2):
+        g.replay()
+        torch.cuda.synchronize()
+        for i in range(3):
+            want = full.decode(np.zeros(1, np.int32), np.array([L + 4 + i], np.int32),
+                               qs[i].cpu().numpy()[None], k_new=k[L + 4 + i][None],
+                               v_new=v[L + 4 + i][None])[0]
+            worst = max(worst, float(np.abs(outs[i].cpu().numpy() - want).max()))
+    del g
+    assert ctx.sync() == 0
+dec.close()
 print(f"rank {rank} max|diff| {worst:.3e}", flush=True)
 dist.destroy_process_group()
 assert worst < 1e-4
 """
 
 
-def test_long_context_split_two_gpus(tmp_path):
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_long_context_split_two_gpus(tmp_path, exchange):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -56,7 +83,7 @@ def test_long_context_split_two_gpus(tmp_path):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    env = dict(os.environ, ROOT=ROOT, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, ROOT=ROOT, NCCL_NVLS_ENABLE="0", EXCHANGE=exchange)
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port",
            str(port), str(script)]

@@ -59,6 +59,12 @@ SIGNATURES = {
     "vxg_attn_cuda_q8_decode_host_async": (_I, [_P, _P, _U, _U, _P, _P, _P, _P, _P, _P, _F, _U,
                                                 _P, _P, _C, _S]),
     "vxg_attn_cuda_ticket_wait": (_I, [_P, ctypes.c_uint64, _C, _S]),
+    "vxg_attn_cuda_peer_buffer_bytes": (_S, [_U, _U, _U]),
+    "vxg_attn_cuda_peer_alloc": (_P, [_P, _U, _U, _U, _P, _C, _S]),
+    "vxg_attn_cuda_peer_open": (_P, [_P, _P, _C, _S]),
+    "vxg_attn_cuda_peer_close": (None, [_P, _P]),
+    "vxg_attn_cuda_peer_free": (None, [_P, _P]),
+    "vxg_attn_cuda_peer_step": (_I, [_P, _P, _U, _U, _U, _U, _P, _P, _P, _P, _C, _S]),
     "vxg_attn_cuda_q8_decode_noalloc": (_I, [_P, _P, _U, _U, _U, _U, _U, _U, _P, _P, _P, _P, _P,
                                              _P, _F, _P, _P, _C, _S]),
     "vxg_attn_cuda_kv_create_f32": (_P, [_P, _U, _U, _U, _U, _C, _S]),

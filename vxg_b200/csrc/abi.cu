@@ -1076,6 +1076,81 @@ int vxg_attn_cuda_lse_combine(void* ctx, uint32_t n_parts, uint32_t n_rows, uint
   });
 }
 
+size_t vxg_attn_cuda_peer_buffer_bytes(uint32_t world, uint32_t n_rows, uint32_t head_dim) {
+  return vxg::peer_buffer_bytes((int)world, (int)(n_rows * (head_dim + 2)));
+}
+
+void* vxg_attn_cuda_peer_alloc(void* ctx, uint32_t world, uint32_t n_rows, uint32_t head_dim,
+                               void* ipc_handle, char* err, size_t cap) {
+  void* p = nullptr;
+  int rc = guarded(ctx, nullptr, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    require(ipc_handle != nullptr, VXG_ATTN_ERR_NULL_PTR, "null ipc_handle");
+    require(world >= 1 && world <= 8 && n_rows > 0 && head_dim > 0, VXG_ATTN_ERR_INVALID_OPTION,
+            "need 1 <= world <= 8 and a non-empty partial");
+    const size_t bytes = vxg_attn_cuda_peer_buffer_bytes(world, n_rows, head_dim);
+    check(cudaMalloc(&p, bytes), "cudaMalloc peer buffer");
+    check(cudaMemset(p, 0, bytes), "cudaMemset peer buffer");
+    cudaIpcMemHandle_t h;
+    check(cudaIpcGetMemHandle(&h, p), "cudaIpcGetMemHandle");
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    (void)c;
+    return VXG_ATTN_OK;
+  });
+  if (rc != VXG_ATTN_OK && p) {
+    cudaFree(p);
+    p = nullptr;
+  }
+  return p;
+}
+
+void* vxg_attn_cuda_peer_open(void* ctx, const void* ipc_handle, char* err, size_t cap) {
+  void* p = nullptr;
+  int rc = guarded(ctx, nullptr, err, cap, [&] {
+    use_ctx(ctx);
+    require(ipc_handle != nullptr, VXG_ATTN_ERR_NULL_PTR, "null ipc_handle");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof(h));
+    check(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    return VXG_ATTN_OK;
+  });
+  return rc == VXG_ATTN_OK ? p : nullptr;
+}
+
+void vxg_attn_cuda_peer_close(void* ctx, void* mapped) {
+  if (!ctx || !mapped) return;
+  cudaSetDevice(static_cast<Ctx*>(ctx)->device);
+  cudaIpcCloseMemHandle(mapped);
+}
+
+void vxg_attn_cuda_peer_free(void* ctx, void* buf) { vxg_attn_cuda_free(ctx, buf); }
+
+int vxg_attn_cuda_peer_step(void* ctx, void* const* bufs, uint32_t world, uint32_t rank,
+                            uint32_t n_rows, uint32_t head_dim, const float* send,
+                            const float* gate, float* out, void* stream, char* err, size_t cap) {
+  return guarded(ctx, stream, err, cap, [&] {
+    Ctx& c = use_ctx(ctx);
+    require(bufs && send && out, VXG_ATTN_ERR_NULL_PTR, "null input");
+    require(world >= 1 && world <= 8 && rank < world, VXG_ATTN_ERR_INVALID_OPTION,
+            "need 1 <= world <= 8 and rank < world");
+    require(n_rows > 0 && head_dim > 0, VXG_ATTN_ERR_INVALID_OPTION, "empty partial");
+    vxg::PeerTable t{};
+    for (uint32_t r = 0; r < world; ++r) {
+      require(bufs[r] != nullptr, VXG_ATTN_ERR_NULL_PTR, "null peer buffer");
+      t.buf[r] = static_cast<float*>(bufs[r]);
+    }
+    require_aligned16(false, {{send, "send"}, {gate, "gate"}, {out, "out"}, {bufs[rank], "buffer"}});
+    cudaStream_t st = pick_stream(c, stream);
+    const int per = (int)(n_rows * (head_dim + 2));
+    check(vxg::launch_peer_push(send, per, t, (int)world, (int)rank, t.buf[rank], st),
+          "peer push launch");
+    check(vxg::launch_peer_combine(t.buf[rank], (int)world, (int)n_rows, (int)head_dim, gate, out,
+                                   c.d_status, st),
+          "peer combine launch");
+    return finish(c, stream, st);
+  });
+}
+
 int vxg_attn_cuda_lse_combine_packed(void* ctx, uint32_t n_parts, uint32_t n_rows,
                                      uint32_t head_dim, const float* packed, const float* gate,
                                      float* out, int memkind, void* stream, char* err,

@@ -157,4 +157,15 @@ cudaError_t launch_gqa_prep(const float* q_raw, float* k_cur, const float* q_nor
                             const float2* rope_cs, int rope_half, int neox, float eps,
                             float* q_out, float* gate_out, cudaStream_t stream);
 
+// peer.cu: long-context partials exchanged over NVLink peer memory
+struct PeerTable {
+  float* buf[8];  // exchange buffer of rank r, as mapped on this GPU (own buffer at `rank`)
+};
+size_t peer_buffer_bytes(int world, int per);
+cudaError_t launch_peer_push(const float* send, int per, const PeerTable& peers, int world,
+                             int rank, float* local_buf, cudaStream_t stream);
+cudaError_t launch_peer_combine(const float* local_buf, int world, int n_rows, int hd,
+                                const float* gate, float* out, uint32_t* status,
+                                cudaStream_t stream);
+
 }  // namespace vxg

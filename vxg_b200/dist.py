@@ -7,7 +7,10 @@
   position, every rank computes the split-KV partial (m, l, o) of the query over its range,
   the partials are all-gathered (NCCL over NVLink on GPUs; any backend works for the host
   logic), and every rank merges them with the log-sum-exp combine.  The exchanged data is
-  n_head * (head_dim + 2) floats per rank, so the collective is latency-bound.
+  n_head * (head_dim + 2) floats per rank, so the collective is latency-bound.  With
+  ``exchange="peer"`` the partials travel through NVLink peer memory instead (PeerExchange:
+  plain stores into every rank's IPC-mapped buffer, a step flag, a bounded wait and the merge,
+  two kernels and no collective per step).
 """
 from __future__ import annotations
 
@@ -68,6 +71,74 @@ def all_gather_partials(m, l, o, group=None):
     return unpack_partials(recv, world, rows, hd)
 
 
+class PeerExchange:
+    """Exchange + log-sum-exp merge of packed partials through NVLink peer memory
+    (vxg_attn_cuda_peer_*): every rank maps every other rank's exchange buffer once (CUDA IPC
+    handles passed with all_gather_object), then each ``step`` is two kernels on the caller's
+    stream and no collective.  Collective over the group: every rank constructs it, steps it
+    the same number of times and closes it."""
+
+    def __init__(self, ctx, world: int, rank: int, n_rows: int, head_dim: int, group=None):
+        import ctypes
+        import torch.distributed as dist
+        from ._lib import ErrBuf, VxgError, lib
+        self.ctx, self.world, self.rank = ctx, world, rank
+        self.n_rows, self.head_dim, self.group = n_rows, head_dim, group
+        err = ErrBuf()
+        handle = (ctypes.c_uint8 * 64)()
+        self._own = lib().vxg_attn_cuda_peer_alloc(ctx.h, world, n_rows, head_dim, handle,
+                                                   err.buf, err.cap)
+        if not self._own:
+            raise VxgError(-7, "vxg_attn_cuda_peer_alloc: " + err.text)
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._mapped = []
+        ptrs = []
+        for r in range(world):
+            if r == rank:
+                ptrs.append(self._own)
+                continue
+            hb = (ctypes.c_uint8 * 64).from_buffer_copy(handles[r])
+            p = lib().vxg_attn_cuda_peer_open(ctx.h, hb, err.buf, err.cap)
+            if not p:
+                raise VxgError(-7, f"vxg_attn_cuda_peer_open(rank {r}): " + err.text)
+            self._mapped.append(p)
+            ptrs.append(p)
+        self._bufs = (ctypes.c_void_p * world)(*ptrs)
+        dist.barrier(group=group)  # every buffer mapped everywhere before the first push
+
+    def step(self, send, out, gate=None, stream=None):
+        """Pushes this rank's packed partials `send` and writes the merged rows to `out`."""
+        import ctypes
+        import torch
+        from ._lib import ErrBuf, check, lib
+        from .attn import _stream_handle
+        s = _stream_handle(stream if stream is not None else torch.cuda.current_stream())
+        err = ErrBuf()
+        check(lib().vxg_attn_cuda_peer_step(
+            self.ctx.h, self._bufs, self.world, self.rank, self.n_rows, self.head_dim,
+            ctypes.c_void_p(send.data_ptr()),
+            ctypes.c_void_p(gate.data_ptr()) if gate is not None else None,
+            ctypes.c_void_p(out.data_ptr()), s, err.buf, err.cap), err)
+        return out
+
+    def close(self):
+        """After every rank's last step: unmap the peers' buffers and free the own one."""
+        import torch
+        import torch.distributed as dist
+        from ._lib import lib
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank still writes into any buffer
+        for p in self._mapped:
+            lib().vxg_attn_cuda_peer_close(self.ctx.h, p)
+        self._mapped = []
+        dist.barrier(group=self.group)  # every mapping of the own buffer is gone
+        lib().vxg_attn_cuda_peer_free(self.ctx.h, self._own)
+        self._own = None
+
+
 class LongContextDecoder:
     """One long sequence split by KV range across the ranks of the default process group.
 
@@ -78,7 +149,7 @@ class LongContextDecoder:
     log-sum-exp combine merges them; all buffers are allocated once."""
 
     def __init__(self, ctx, capacity: int, n_head: int, n_head_kv: int, head_dim: int,
-                 world: int, rank: int, group=None):
+                 world: int, rank: int, group=None, exchange: str = "nccl"):
         from .attn import KvQ8Pool
         import torch
         self.ctx = ctx
@@ -98,6 +169,15 @@ class LongContextDecoder:
         self._m = self._send[:n_head].view(1, n_head)
         self._l = self._send[n_head:2 * n_head].view(1, n_head)
         self._o = self._send[2 * n_head:].view(1, n_head, head_dim)
+        if exchange not in ("nccl", "peer"):
+            raise ValueError("exchange must be 'nccl' or 'peer'")
+        self.peer = PeerExchange(ctx, world, rank, n_head, head_dim, group) \
+            if exchange == "peer" else None
+
+    def close(self):
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def step(self, pos: int, q, k_new, v_new, scale=None):
         """Append (k_new, v_new) at ``pos`` (on its owner) and attend q over [0, pos]."""
@@ -112,6 +192,8 @@ class LongContextDecoder:
         self.pool.decode_partial(self._seq, self._begin, self._end,
                                  q.reshape(1, self.n_head, self.head_dim), scale=scale,
                                  out=(self._m, self._l, self._o))
+        if self.peer is not None:
+            return self.peer.step(self._send, self._out)
         dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
         return lse_combine_packed(self.ctx, self._recv, self.world, self.n_head, self.head_dim,
                                   out=self._out)
