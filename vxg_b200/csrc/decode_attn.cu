@@ -155,6 +155,7 @@ constexpr int REC = NB * kBlk;     // 272 B per (token, kv head)
 constexpr int TOKB = NKV * REC;    // 544 B per token in one cache
 constexpr int ST = 96;             // tokens per unit / stage
 constexpr int NS = 2;              // stages in flight
+constexpr int CPS = 1;             // CTAs per SM (each with its own stage ring)
 constexpr int STB = ST * TOKB;     // bytes per stage per cache (52224 at ST = 96)
 constexpr int SPK = ST / 16;       // 16-token sub-tiles per kv head in a stage
 constexpr int WPS = NKV * SPK;     // warps working on one stage
@@ -287,7 +288,7 @@ __device__ __forceinline__ UnitInfo unit_info(const DecodeArgs& a, const int* pr
 // the end of a (batch entry, CTA) segment every warp writes its own (m, l, O) partial; the
 // combine kernel merges them.  Partial slot of warp (kh, sub) in CTA i for entry b:
 // (i + b) * SUBS + sub, heads kh*8 .. kh*8+7, O stored [dim][head].
-__global__ void __launch_bounds__(fast::THREADS, 1) decode_fast_split(DecodeArgs a,
+__global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(DecodeArgs a,
                                                                        Partials part) {
   using namespace fast;
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -674,7 +675,7 @@ __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partial
                                                            float* o_out) {
   using namespace fast;
   constexpr int H = NKV * G;
-  constexpr int MAXS = 256 * SUBS;
+  constexpr int MAXS = 512 * SUBS;  // every split CTA may meet the entry (grid <= 512)
   const int b = blockIdx.x, z = blockIdx.z;
   const int tid = threadIdx.x, dl = tid % kCombineDims, sl = tid / kCombineDims;
   const int d = blockIdx.y * kCombineDims + dl;
@@ -921,7 +922,7 @@ int generic_max_split(const DecodeArgs& a) {
 
 namespace {
 // CTAs of the persistent split pass (the combine stages their unit ranges: at most 512).
-int fast_grid(int sm_count) { return std::max(1, std::min(sm_count, 512)); }
+int fast_grid(int sm_count) { return std::max(1, std::min(fast::CPS * sm_count, 512)); }
 // Slot splits of the fast combine: aim for >= 128 CTAs of 64 output dims each.
 int combine_splits(const DecodeArgs& a) {
   const int per = std::max(1, a.n_batch * (fast::HD / kCombineDims));
@@ -931,18 +932,18 @@ int combine_splits(const DecodeArgs& a) {
 
 size_t decode_partial_floats(const DecodeArgs& a, int sm_count) {
   size_t slots;
-  if (fast_applies(a)) slots = ((size_t)sm_count + a.n_batch) * fast::SUBS;
+  if (fast_applies(a)) slots = ((size_t)fast_grid(sm_count) + a.n_batch) * fast::SUBS;
   else slots = (size_t)a.n_batch * generic_max_split(a);
   size_t f = slots * a.n_head * (2 + (size_t)a.nb * 32);
   const int S = fast_applies(a) ? combine_splits(a) : 1;
   if (S > 1) f += (size_t)a.n_batch * S * a.n_head * (2 + fast::HD);
-  if (fast_applies(a)) f += (size_t)a.n_batch + sm_count + 64;  // published prefix + CTA ranges
+  if (fast_applies(a)) f += (size_t)a.n_batch + fast_grid(sm_count) + 64;  // prefix + CTA ranges
   return f;
 }
 
 Partials carve_partials(float* base, const DecodeArgs& a, int sm_count) {
   size_t slots;
-  if (fast_applies(a)) slots = ((size_t)sm_count + a.n_batch) * fast::SUBS;
+  if (fast_applies(a)) slots = ((size_t)fast_grid(sm_count) + a.n_batch) * fast::SUBS;
   else slots = (size_t)a.n_batch * generic_max_split(a);
   Partials p;
   p.m = base;
