@@ -7,7 +7,7 @@
 // tiles of 32, 16 warps with fixed roles:
 //   warp 0       loader: one 2-D TMA tensor copy per cache and tile (this kv head's 272-byte
 //                Q8 records of 32 tokens) from the KV pool into a 3-deep raw ring;
-//   warp 1       MMA issuer (one thread) and TMEM owner;
+//   warp 1       QK MMA issuer (one thread) and TMEM owner; warp 13: PV MMA issuer (one thread);
 //   warps 4-7    softmax: thread = query row = TMEM lane; also Q -> TMEM and the epilogue;
 //   warps 2, 3, 8, 10, 11, 12, 14, 15   converters: Q8 records -> f16 hi/lo planes (K and V)
 //                in 128-byte-swizzled shared memory, double-buffered separately for K and V.
@@ -54,7 +54,7 @@ struct __align__(1024) Smem {
   // the softmax that S (resp. O) is ready and the converters that the K (resp. V) planes of
   // stage i & 1 are free
   uint64_t qk_done[2], pv_done[2];
-  uint64_t q_full, drain;
+  uint64_t q_full, drain[2];   // drain[0]: QK issuer, drain[1]: PV issuer
   uint32_t tmem;
   volatile int abort;
 };
@@ -97,7 +97,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
 }
 
 // Warp w issues on scheduler w % 4.  The converters sit on warps 2, 3, 8, 10, 11, 12, 14, 15, so
-// the MMA-issuing warp 1 shares its scheduler only with softmax warp 5 (warps 9 and 13 idle).
+// the MMA-issuing warps 1 and 13 share their scheduler only with softmax warp 5 (warp 9 idle).
 __device__ __forceinline__ int conv_index(int warp) {
   const int v = (int)((0x76f543f2ffff10ffull >> (4 * warp)) & 0xf);
   return v == 15 ? -1 : v;
@@ -206,7 +206,8 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
       mbar_init(&sm.p_full[i], ROWS);
     }
     mbar_init(&sm.q_full, ROWS);
-    mbar_init(&sm.drain, 1);
+    mbar_init(&sm.drain[0], 1);
+    mbar_init(&sm.drain[1], 1);
     sm.abort = 0;
     fence_mbar_init();
   }
@@ -237,25 +238,51 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
+    // ---------------------------------------------------------------- QK issuer
+    // Two threads issue the MMAs: this one the QK products, warp 13's the PV products, each
+    // waiting only for its own inputs, so a late P or late V planes do not hold back the next
+    // tile's QK (and a late K tile does not hold back a PV).  QK of tile j + 2 overwrites the S
+    // buffer that held P of tile j: it waits for that PV to complete first.
     if (lane == 0) {
       const uint32_t id_qk = tc::idesc_f16(128, 2 * KT, false);
-      const uint32_t id_pv = tc::idesc_f16(128, HD, true);
       bool ok = wait_or_abort(&sm.q_full, 0, sm, status);
       tc::fence_after_sync();
       // Descriptors are built once; a K-step only adds its byte offset >> 4 to the start-address
       // field (the stage buffers lie far below the field's 256 KB limit), so issuing an MMA
-      // costs a few instructions: this thread shares its scheduler with busy warps.
+      // costs a few instructions.
       const uint64_t kd0 = tc::sdesc_sw128(smem_u32(sm.kpl[0]), 16, 1024);
       const uint64_t kd1 = tc::sdesc_sw128(smem_u32(sm.kpl[1]), 16, 1024);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int st = j & 1;
+        if (!wait_or_abort(&sm.kf[st], (j >> 1) & 1, sm, status)) break;
+        if (j >= 2 && !wait_or_abort(&sm.pv_done[st], ((j >> 1) - 1) & 1, sm, status)) break;
+        tc::fence_after_sync();
+        const uint64_t kd = st ? kd1 : kd0;
+        const uint32_t sd = tm + TM_S + 2 * KT * st;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t koff = (kk >> 2) * (2 * KT * 128) + (kk & 3) * 32;  // compile-time
+          tc::mma_ts(sd, tm + TM_Q + kk * 8, kd + (uint64_t)(koff >> 4), id_qk, kk > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(&sm.qk_done[st]);
+      }
+      // drain: every MMA issued here is done before the TMEM is released
+      tc::mma_commit(&sm.drain[0]);
+      mbar_wait(&sm.drain[0], 0, kWaitNs);
+    }
+    __syncwarp();
+  } else if (warp == 13) {
+    // ---------------------------------------------------------------- PV issuer
+    if (lane == 0) {
+      const uint32_t id_pv = tc::idesc_f16(128, HD, true);
       const uint64_t vh0 = tc::sdesc_sw128(smem_u32(sm.vpl[0][0]), KT * 128, 1024);
       const uint64_t vh1 = tc::sdesc_sw128(smem_u32(sm.vpl[1][0]), KT * 128, 1024);
       const uint64_t vl0 = tc::sdesc_sw128(smem_u32(sm.vpl[0][1]), KT * 128, 1024);
       const uint64_t vl1 = tc::sdesc_sw128(smem_u32(sm.vpl[1][1]), KT * 128, 1024);
-      auto pv = [&](int i) -> bool {
+      for (int i = 0; i < n_tiles; ++i) {
         const int st = i & 1;
-        if (!wait_or_abort(&sm.vf[st], (i >> 1) & 1, sm, status)) return false;
-        if (!wait_or_abort(&sm.p_full[st], (i >> 1) & 1, sm, status)) return false;
+        if (!wait_or_abort(&sm.vf[st], (i >> 1) & 1, sm, status)) break;
+        if (!wait_or_abort(&sm.p_full[st], (i >> 1) & 1, sm, status)) break;
         tc::fence_after_sync();
         const uint32_t ph = tm + TM_S + 2 * KT * st, pl = ph + 16;
         const uint64_t vh = st ? vh1 : vh0, vl = st ? vl1 : vl0;
@@ -269,26 +296,9 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
           tc::mma_ts(tm + TM_O, pl + kk * 8, dh, id_pv, 1u);
         }
         tc::mma_commit(&sm.pv_done[st]);
-        return true;
-      };
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int st = j & 1;
-        if (!wait_or_abort(&sm.kf[st], (j >> 1) & 1, sm, status)) { ok = false; break; }
-        tc::fence_after_sync();
-        const uint64_t kd = st ? kd1 : kd0;
-        const uint32_t sd = tm + TM_S + 2 * KT * st;
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * (2 * KT * 128) + (kk & 3) * 32;  // compile-time
-          tc::mma_ts(sd, tm + TM_Q + kk * 8, kd + (uint64_t)(koff >> 4), id_qk, kk > 0 ? 1u : 0u);
-        }
-        tc::mma_commit(&sm.qk_done[st]);
-        if (j > 0 && !pv(j - 1)) { ok = false; break; }
       }
-      if (ok && n_tiles > 0) pv(n_tiles - 1);
-      // drain: wait for every MMA issued above before the TMEM is released
-      tc::mma_commit(&sm.drain);
-      mbar_wait(&sm.drain, 0, kWaitNs);
+      tc::mma_commit(&sm.drain[1]);
+      mbar_wait(&sm.drain[1], 0, kWaitNs);
     }
     __syncwarp();
   } else if (warp >= 4 && warp < 8) {
