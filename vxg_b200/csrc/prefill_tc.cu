@@ -9,7 +9,7 @@
 //                Q8 records of 32 tokens) from the KV pool into a 3-deep raw ring;
 //   warp 1       QK MMA issuer (one thread) and TMEM owner; warp 13: PV MMA issuer (one thread);
 //   warps 4-7    softmax: thread = query row = TMEM lane; also Q -> TMEM and the epilogue;
-//   warps 2, 3, 8, 10, 11, 12, 14, 15   converters: Q8 records -> f16 hi/lo planes (K and V)
+//   warps 2, 3, 8, 10 / 11, 12, 14, 15   K / V converters: Q8 records -> f16 hi/lo planes
 //                in 128-byte-swizzled shared memory, double-buffered separately for K and V.
 // Tensor memory (512 columns): O [0,256) f32, Q [256,384) f16 pairs, S0/S1 [384,512) f32.  The
 // K hi and lo planes are stacked as 64 B-rows, so one MMA per K-step gives both halves of S:
@@ -199,8 +199,8 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
       mbar_init(&sm.raw_empty[i], 8);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.kf[i], 8);
-      mbar_init(&sm.vf[i], 8);
+      mbar_init(&sm.kf[i], 4);
+      mbar_init(&sm.vf[i], 4);
       mbar_init(&sm.qk_done[i], 1);
       mbar_init(&sm.pv_done[i], 1);
       mbar_init(&sm.p_full[i], ROWS);
@@ -433,32 +433,41 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
     }
   } else if (conv_index(warp) >= 0) {
     // ---------------------------------------------------------------- converters
-    // Lane -> (key, 32-dim block): 8 keys x blocks {0,2,4,6} (converters 0-3) or {1,3,5,7}
-    // (converters 4-7).  Record rows are 68 words apart, so 8 keys start in 8 banks = 0 mod 4, and
-    // those four blocks start at word offsets 0, 1, 2, 3 mod 4: the 32 lanes read 32 distinct
-    // banks, and the swizzled 16-byte stores of 8 keys cover all banks once per block.
+    // Converters 0-3 make the K planes, converters 4-7 the V planes, each thread two (key,
+    // 32-dim block) items per tile, so K conversion of the next tile does not wait behind V
+    // conversion (which waits for the PV that frees its planes).  Lane -> key 8 w + lane % 8 and
+    // blocks {0,2,4,6} or {1,3,5,7}: record rows are 68 words apart, so 8 keys start in 8 banks =
+    // 0 mod 4 and those four blocks at word offsets 0, 1, 2, 3 mod 4: the 32 lanes read 32
+    // distinct banks, and the swizzled 16-byte stores of 8 keys cover all banks once per block.
     const int wc = conv_index(warp);
+    const bool is_k = wc < 4;
     const int key = 8 * (wc & 3) + (lane & 7);
-    const int c = 2 * (lane >> 3) + (wc >> 2);
+    const int c = 2 * (lane >> 3);
+    uint64_t* free_bar = is_k ? sm.qk_done : sm.pv_done;
+    uint64_t* full_bar = is_k ? sm.kf : sm.vf;
     for (int j = 0; j < n_tiles; ++j) {
       const int rs = j % NRAW, st = j & 1;
       if (!wait_or_abort(&sm.raw_full[rs], (j / NRAW) & 1, sm, status)) break;
       const bool valid = j * KT + key < key_end;
-      // K planes of stage st are free once QK of tile j-2 is done
-      if (j >= 2 && !wait_or_abort(&sm.qk_done[st], ((j >> 1) - 1) & 1, sm, status)) break;
-      pftc::convert_block(sm.raw[rs][0] + key * REC + c * kBlk, sm.kpl[st],
-                          sm.kpl[st] + KT * 128, 2 * KT * 128, key, c, valid);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&sm.kf[st]);
-      // V planes of stage st are free once PV of tile j-2 is done
-      if (j >= 2 && !wait_or_abort(&sm.pv_done[st], ((j >> 1) - 1) & 1, sm, status)) break;
-      pftc::convert_block(sm.raw[rs][1] + key * REC + c * kBlk, sm.vpl[st][0], sm.vpl[st][1],
-                          KT * 128, key, c, valid);
+      // the planes of stage st are free once the QK (K) or PV (V) of tile j - 2 is done
+      if (j >= 2 && !wait_or_abort(&free_bar[st], ((j >> 1) - 1) & 1, sm, status)) break;
+      if (is_k) {
+        const uint8_t* rec = sm.raw[rs][0] + key * REC;
+        pftc::convert_block(rec + c * kBlk, sm.kpl[st], sm.kpl[st] + KT * 128, 2 * KT * 128, key,
+                            c, valid);
+        pftc::convert_block(rec + (c + 1) * kBlk, sm.kpl[st], sm.kpl[st] + KT * 128, 2 * KT * 128,
+                            key, c + 1, valid);
+      } else {
+        const uint8_t* rec = sm.raw[rs][1] + key * REC;
+        pftc::convert_block(rec + c * kBlk, sm.vpl[st][0], sm.vpl[st][1], KT * 128, key, c,
+                            valid);
+        pftc::convert_block(rec + (c + 1) * kBlk, sm.vpl[st][0], sm.vpl[st][1], KT * 128, key,
+                            c + 1, valid);
+      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tc::mbar_arrive(&sm.vf[st]);
+        tc::mbar_arrive(&full_bar[st]);
         tc::mbar_arrive(&sm.raw_empty[rs]);
       }
     }
