@@ -305,7 +305,8 @@ __global__ void __launch_bounds__(256, 1) deltanet_step_persistent(DeltaNetArgs 
 // Preparation pass: normalised q, k per (b, t, k head) and (beta, decay) per (b, t, v head).
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) deltanet_prep_kernel(DeltaNetArgs a, float* qn, float* kn,
-                                                            float2* gates, float* lgs) {
+                                                            float2* gates, float* lgs,
+                                                            float q_scale) {
   // blockIdx.x = (b * n_tok + t) ; threads cover the k heads (warp per head) then the gates
   const int bt = blockIdx.x;
   const int b = bt / a.n_tok, t = bt - b * a.n_tok;
@@ -320,7 +321,7 @@ __global__ void __launch_bounds__(128) deltanet_prep_kernel(DeltaNetArgs a, floa
     }
     sq = warp_sum(sq);
     sk = warp_sum(sk);
-    const float qs = a.q_scale / sqrtf(sq + a.eps), ks = 1.0f / sqrtf(sk + a.eps);
+    const float qs = q_scale / sqrtf(sq + a.eps), ks = 1.0f / sqrtf(sk + a.eps);
     float* qo = qn + ((size_t)bt * a.n_kh + hk) * a.dk;
     float* ko = kn + ((size_t)bt * a.n_kh + hk) * a.dk;
     for (int i = lane; i < a.dk; i += 32) {
@@ -340,7 +341,7 @@ __global__ void __launch_bounds__(128) deltanet_prep_kernel(DeltaNetArgs a, floa
 // rows with 16-byte aligned starts (dk <= 256); the gates take one thread per (b, t, v head).
 __global__ void __launch_bounds__(256) deltanet_prep_vec_kernel(DeltaNetArgs a, float* qn,
                                                                 float* kn, float2* gates,
-                                                                float* lgs) {
+                                                                float* lgs, float q_scale) {
   const int lane = threadIdx.x & 31;
   const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (w < (long long)a.n_batch * a.n_tok * a.n_kh) {
@@ -366,7 +367,7 @@ __global__ void __launch_bounds__(256) deltanet_prep_vec_kernel(DeltaNetArgs a, 
     }
     sq = warp_sum(sq);
     sk = warp_sum(sk);
-    const float qs = a.q_scale / sqrtf(sq + a.eps), ks = 1.0f / sqrtf(sk + a.eps);
+    const float qs = q_scale / sqrtf(sq + a.eps), ks = 1.0f / sqrtf(sk + a.eps);
     float* qo = qn + ((size_t)bt * a.n_kh + hk) * a.dk;
     float* ko = kn + ((size_t)bt * a.n_kh + hk) * a.dk;
 #pragma unroll
@@ -553,6 +554,9 @@ cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, int al
   float2* gates = reinterpret_cast<float2*>(kn + bt * a.n_kh * a.dk);
   float* lgs = reinterpret_cast<float*>(gates + bt * a.n_vh);
   const bool chunked = allow_chunk && deltanet_chunk_supported(a);
+  // the chunked kernel takes q unit-normalised (its f16 products want |q| <= 1) and applies
+  // q_scale to the products; the sequential kernel takes it folded in
+  const float qscale = chunked ? 1.0f : a.q_scale;
   const bool vec = a.dk % 4 == 0 && a.dk <= 256 && a.q_ts % 4 == 0 && a.q_bs % 4 == 0 &&
                    a.k_ts % 4 == 0 && a.k_bs % 4 == 0 &&
                    ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k)) & 15u) == 0;
@@ -560,9 +564,10 @@ cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, int al
     const long long warps = (long long)bt * a.n_kh, gthreads = (long long)bt * a.n_vh;
     const long long blocks = std::max((warps + 7) / 8, (gthreads + 255) / 256);
     deltanet_prep_vec_kernel<<<(unsigned)blocks, 256, 0, st>>>(a, qn, kn, gates,
-                                                              chunked ? lgs : nullptr);
+                                                              chunked ? lgs : nullptr, qscale);
   } else {
-    deltanet_prep_kernel<<<(unsigned)bt, 128, 0, st>>>(a, qn, kn, gates, chunked ? lgs : nullptr);
+    deltanet_prep_kernel<<<(unsigned)bt, 128, 0, st>>>(a, qn, kn, gates, chunked ? lgs : nullptr,
+                                                       qscale);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

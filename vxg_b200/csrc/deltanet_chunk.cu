@@ -9,11 +9,12 @@
 //   O  = diag(gamma) Q S0^T + (M o Q K^T) W,   M[t][i] = exp(L_t - L_i) for i <= t
 //   S_C = gamma_C S0 + W^T diag(exp(L_C - L)) K
 // which is the same recurrence re-associated.  One CTA = (sequence, v head, 64 rows of the
-// state), chunks in order, state rows on chip.  The products run on mma.sync m16n8k8 TF32 with
-// f32 accumulation; the triangular solve's products and the state update use 3xTF32 (hi/lo
-// operand splits), which keeps the result within a few % of the 1e-3 bar of the sequential fp32
-// recurrence at 8192 tokens (the single-pass products contribute that; the state update and
-// the solve would otherwise dominate).
+// state), chunks in order, state rows on chip.  The products run on mma.sync m16n8k16 with f32
+// accumulation, each in the operand format its accuracy needs (measured against the sequential
+// f32 recurrence at 8192 tokens): K K^T and Q K^T in f16 (q and k are L2-normalised, |x| <= 1,
+// and q's scale is applied to the products); K S0^T in bf16; Q S0^T, P W, the triangular solve
+// and the state update in hi/lo-split bf16 (BF16X3), which keeps the f32 exponent range for the
+// unbounded state and W.  Operands stay f32 in shared memory and are converted per fragment.
 #include "kernels.h"
 
 namespace vxg {
@@ -23,11 +24,12 @@ constexpr int C = 64;        // chunk length
 constexpr int DK = 128;
 constexpr int DS = 64;       // state rows (v dims) per CTA
 constexpr int THREADS = 256;
-// Row strides (floats).  Matrices read along k (contiguous) take 64-bit fragment loads and want
-// a stride of 8 mod 32; R, read along its rows by most products, wants 4 mod 32.
+// Row strides (floats), chosen for conflict-free fragment loads (see KOrder): K, Q, S (PAIR
+// loads, and SPREAD loads along k for the state update) and R (SPREAD loads along k) want 8
+// mod 32; A / T and P (SPREAD loads along their rows) want 4 mod 32.
 constexpr int LDK = DK + 8;       // K, Q, S
-constexpr int LDR = DS + 4;       // R: V rows -> right-hand side -> W
-constexpr int LDA = C + 8;        // A / T, P
+constexpr int LDR = DS + 8;       // R: V rows -> right-hand side -> W
+constexpr int LDA = C + 4;        // A / T, P
 
 struct __align__(16) Smem {
   float k[2][C][LDK];  // chunk c in k[c & 1]; chunk c + 1 lands in the other while c computes
@@ -41,20 +43,6 @@ struct __align__(16) Smem {
   float gam[C];      // exp(L_t)
   float rdec[C];     // exp(L_C - L_t)
 };
-
-__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-// f32 -> (hi, lo) with hi the top 19 bits (what the TF32 datapath reads) and lo = x - hi exact
-__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  hi = __float_as_uint(x) & 0xFFFFE000u;
-  lo = __float_as_uint(x - __uint_as_float(hi));
-}
 
 // 16-byte asynchronous global -> shared copy (zero fill when !valid; src must stay a valid
 // address), committed as one group per call site and awaited with cp_async_wait_all.
@@ -70,70 +58,133 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
-// acc[nt] (+)= A(m0.., k) B(k, n0 + 8 nt ..) over k in [k0, k1): one 16-row tile, NT 8-col
-// tiles.  A is [m][k] (AK) or [k][m]; B is [n][k] (BK) or [k][n]; ascale (optional) scales A's
-// column k.  Operands go to the TF32 datapath as raw f32 bits (it reads the top 19); X3 adds the
-// hi/lo correction products.  Inside each 8-wide k step, fragment slot q holds k + 2q and slot
-// q + 4 holds k + 2q + 1 (the same permutation for A and B), so k-contiguous operands load as
-// 64-bit pairs.
-template <int NT, bool X3, bool AK, bool BK>
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// two f32 -> one register of two 16-bit values, x0 in the low half (the lower k index)
+__device__ __forceinline__ uint32_t pack_f16(float x0, float x1) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_bf16(float x0, float x1) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// (x0, x1) -> bf16 pairs hi = rn(x), lo = rn(x - hi); hi + lo carries 16 significant bits
+__device__ __forceinline__ void split_bf16(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16(x0, x1);
+  lo = pack_bf16(x0 - __uint_as_float(hi << 16), x1 - __uint_as_float(hi & 0xFFFF0000u));
+}
+
+// Operand formats of a product.  F16: one f16 pass, for the normalised q / k (|x| <= 1, so no
+// range loss).  BF16: one bf16 pass.  BF16X3: hi/lo bf16 splits of both operands and the three
+// products hi.hi + hi.lo + lo.hi (16 significant bits per operand, the f32 exponent range).
+enum Fmt { F16, BF16, BF16X3 };
+// k orders of a 16-wide k step.  The MMA's k slots of lane quad q are 2q, 2q+1 (a0/a1, b0) and
+// 2q+8, 2q+9 (a2/a3, b1); any permutation of k applied to both operands leaves the product
+// unchanged.  PAIR keeps slot = k, so a k-contiguous operand loads as 64-bit pairs (row
+// strides of 8 mod 32 words are conflict-free).  SPREAD maps slots 2q+j -> q+4j and
+// 2q+8+j -> q+8+4j: scalar loads, conflict-free for a [k][m|n] operand with row stride 8 mod 32
+// and for an [m|n][k] operand with row stride 4 mod 32.
+enum KOrder { PAIR, SPREAD };
+
+// acc[nt] (+)= A(m0.., k) B(k, n0 + 8 nt ..) over k in [k0, k1) (multiple of 16): one 16-row
+// tile, NT 8-col tiles.  A is [m][k] (AK) or [k][m]; B is [n][k] (BK) or [k][n]; ascale
+// (optional) scales A's column k.  SEP keeps the two BF16X3 correction products in their own
+// accumulators (shorter dependency chains for small NT).
+template <int NT, Fmt FMT, KOrder KO, bool AK, bool BK, bool SEP = false>
 __device__ __forceinline__ void warp_mma(float (&acc)[NT][4], const float* A, int lda,
                                          const float* B, int ldb, int m0, int n0, int k0, int k1,
                                          const float* ascale = nullptr) {
+  static_assert(KO == SPREAD || (AK && BK), "PAIR order needs k-contiguous operands");
   const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-  // the two correction products accumulate separately: three short dependency chains per tile
-  float c1[X3 ? NT : 1][4], c2[X3 ? NT : 1][4];
+  constexpr bool X3 = FMT == BF16X3;
+  float c1[X3 && SEP ? NT : 1][4], c2[X3 && SEP ? NT : 1][4];
 #pragma unroll
-  for (int i = 0; i < (X3 ? NT : 1); ++i)
+  for (int i = 0; i < (X3 && SEP ? NT : 1); ++i)
 #pragma unroll
     for (int e = 0; e < 4; ++e) c1[i][e] = c2[i][e] = 0.f;
-  for (int k = k0; k < k1; k += 8) {
-    const int kk = k + 2 * q;
-    float a[4];
-    if constexpr (AK) {
-      const float2 r0 = *reinterpret_cast<const float2*>(A + (m0 + g) * lda + kk);
-      const float2 r1 = *reinterpret_cast<const float2*>(A + (m0 + g + 8) * lda + kk);
-      a[0] = r0.x; a[2] = r0.y; a[1] = r1.x; a[3] = r1.y;
-    } else {
-      a[0] = A[kk * lda + m0 + g];
-      a[2] = A[(kk + 1) * lda + m0 + g];
-      a[1] = A[kk * lda + m0 + g + 8];
-      a[3] = A[(kk + 1) * lda + m0 + g + 8];
+  // physical k of slots (2q, 2q+1, 2q+8, 2q+9)
+  const int o0 = KO == PAIR ? 2 * q : q, o1 = KO == PAIR ? 2 * q + 1 : q + 4;
+  const int o2 = o0 + 8, o3 = o1 + 8;
+  for (int k = k0; k < k1; k += 16) {
+    float x[2][4];  // rows g, g + 8; slots 0..3
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int m = m0 + g + 8 * h;
+      if constexpr (KO == PAIR) {
+        const float2 r0 = *reinterpret_cast<const float2*>(A + m * lda + k + o0);
+        const float2 r1 = *reinterpret_cast<const float2*>(A + m * lda + k + o2);
+        x[h][0] = r0.x; x[h][1] = r0.y; x[h][2] = r1.x; x[h][3] = r1.y;
+      } else if constexpr (AK) {
+        x[h][0] = A[m * lda + k + o0]; x[h][1] = A[m * lda + k + o1];
+        x[h][2] = A[m * lda + k + o2]; x[h][3] = A[m * lda + k + o3];
+      } else {
+        x[h][0] = A[(k + o0) * lda + m]; x[h][1] = A[(k + o1) * lda + m];
+        x[h][2] = A[(k + o2) * lda + m]; x[h][3] = A[(k + o3) * lda + m];
+      }
+      if (ascale) {
+        x[h][0] *= ascale[k + o0]; x[h][1] *= ascale[k + o1];
+        x[h][2] *= ascale[k + o2]; x[h][3] *= ascale[k + o3];
+      }
     }
-    if (ascale) {
-      const float s0 = ascale[kk], s1 = ascale[kk + 1];
-      a[0] *= s0; a[1] *= s0; a[2] *= s1; a[3] *= s1;
-    }
+    // a0 = row g slots 0,1; a1 = row g+8 slots 0,1; a2 = row g slots 2,3; a3 = row g+8 slots 2,3
     uint32_t ah[4], al[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if constexpr (X3) split_tf32(a[i], ah[i], al[i]);
-      else ah[i] = __float_as_uint(a[i]);
+    for (int r = 0; r < 4; ++r) {
+      const int h = r & 1, s0 = (r >> 1) * 2;
+      if constexpr (FMT == F16) ah[r] = pack_f16(x[h][s0], x[h][s0 + 1]);
+      else if constexpr (FMT == BF16) ah[r] = pack_bf16(x[h][s0], x[h][s0 + 1]);
+      else split_bf16(x[h][s0], x[h][s0 + 1], ah[r], al[r]);
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int n = n0 + 8 * nt + g;
-      float b0, b1;
-      if constexpr (BK) {
-        const float2 r = *reinterpret_cast<const float2*>(B + n * ldb + kk);
-        b0 = r.x; b1 = r.y;
+      float y[4];
+      if constexpr (KO == PAIR) {
+        const float2 r0 = *reinterpret_cast<const float2*>(B + n * ldb + k + o0);
+        const float2 r1 = *reinterpret_cast<const float2*>(B + n * ldb + k + o2);
+        y[0] = r0.x; y[1] = r0.y; y[2] = r1.x; y[3] = r1.y;
+      } else if constexpr (BK) {
+        y[0] = B[n * ldb + k + o0]; y[1] = B[n * ldb + k + o1];
+        y[2] = B[n * ldb + k + o2]; y[3] = B[n * ldb + k + o3];
       } else {
-        b0 = B[kk * ldb + n];
-        b1 = B[(kk + 1) * ldb + n];
+        y[0] = B[(k + o0) * ldb + n]; y[1] = B[(k + o1) * ldb + n];
+        y[2] = B[(k + o2) * ldb + n]; y[3] = B[(k + o3) * ldb + n];
       }
-      if constexpr (X3) {
-        uint32_t bh0, bl0, bh1, bl1;
-        split_tf32(b0, bh0, bl0);
-        split_tf32(b1, bh1, bl1);
-        mma_tf32(c1[nt], al, bh0, bh1);
-        mma_tf32(c2[nt], ah, bl0, bl1);
-        mma_tf32(acc[nt], ah, bh0, bh1);
+      if constexpr (FMT == F16) {
+        mma_f16(acc[nt], ah, pack_f16(y[0], y[1]), pack_f16(y[2], y[3]));
+      } else if constexpr (FMT == BF16) {
+        mma_bf16(acc[nt], ah, pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]));
       } else {
-        mma_tf32(acc[nt], ah, __float_as_uint(b0), __float_as_uint(b1));
+        uint32_t bh0, bl0, bh1, bl1;
+        split_bf16(y[0], y[1], bh0, bl0);
+        split_bf16(y[2], y[3], bh1, bl1);
+        if constexpr (SEP) {
+          mma_bf16(c1[nt], al, bh0, bh1);
+          mma_bf16(c2[nt], ah, bl0, bl1);
+        } else {
+          mma_bf16(acc[nt], al, bh0, bh1);
+          mma_bf16(acc[nt], ah, bl0, bl1);
+        }
+        mma_bf16(acc[nt], ah, bh0, bh1);
       }
     }
   }
-  if constexpr (X3)
+  if constexpr (X3 && SEP)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -256,7 +307,7 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
     {
       float acc[4][4];
       zero(acc);
-      warp_mma<4, false, true, true>(acc, &kb[0][0], LDK, &kb[0][0], LDK, 16 * mt,
+      warp_mma<4, F16, PAIR, true, true>(acc, &kb[0][0], LDK, &kb[0][0], LDK, 16 * mt,
                                      32 * half, 0, DK);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
@@ -266,7 +317,7 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
           sm.a[t][i] = i < t ? sm.beta[t] * expf(sm.L[t] - sm.L[i]) * acc[nt][e] : 0.f;
         }
       zero(acc);
-      warp_mma<4, false, true, true>(acc, &kb[0][0], LDK, &sm.s[0][0], LDK, 16 * mt,
+      warp_mma<4, BF16, PAIR, true, true>(acc, &kb[0][0], LDK, &sm.s[0][0], LDK, 16 * mt,
                                      32 * half, 0, DK);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
@@ -279,18 +330,16 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
     __syncthreads();
     if (warp < 4) {
       // ---- diagonal 16x16 block `warp` of T = (I + A)^-1 in place; lane j = column j -------
+      // Right-looking forward substitution: once x[r] is final it updates every later row, so
+      // the dependency chain is one FMA per row (entries above row j stay 0 without masking).
       const int j = lane & 15, o = 16 * warp;
       float col[16];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        float v = r == j ? 1.f : 0.f;
-        if (r > j) {
+      for (int r = 0; r < 16; ++r) col[r] = r == j ? 1.f : 0.f;
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (i >= j && i < r) v = fmaf(-sm.a[o + r][o + i], col[i], v);
-        }
-        col[r] = v;
-      }
+      for (int r = 0; r < 15; ++r)
+#pragma unroll
+        for (int i = r + 1; i < 16; ++i) col[i] = fmaf(-sm.a[o + i][o + r], col[r], col[i]);
       __syncwarp();
       if (lane < 16)
 #pragma unroll
@@ -300,13 +349,13 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
       const int m = warp - 4;
       float acc[8][4];
       zero(acc);
-      warp_mma<8, false, true, true>(acc, &sm.q[0][0], LDK, &kb[0][0], LDK, 16 * m, 0, 0, DK);
+      warp_mma<8, F16, PAIR, true, true>(acc, &sm.q[0][0], LDK, &kb[0][0], LDK, 16 * m, 0, 0, DK);
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int t = 16 * m + g + (e >> 1) * 8, i = 8 * nt + 2 * qd + (e & 1);
-          sm.p[t][i] = i <= t ? expf(sm.L[t] - sm.L[i]) * acc[nt][e] : 0.f;
+          sm.p[t][i] = i <= t ? expf(sm.L[t] - sm.L[i]) * (acc[nt][e] * a.q_scale) : 0.f;
         }
     }
     __syncthreads();
@@ -318,8 +367,8 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
         float acc[2][4];
         zero(acc);
         if (bi > 0)
-          warp_mma<2, true, true, false>(acc, &sm.a[0][0], LDA, &rb[0][0], LDR, 16 * bi, n0,
-                                         0, 16 * bi);
+          warp_mma<2, BF16X3, SPREAD, true, false, true>(acc, &sm.a[0][0], LDA, &rb[0][0], LDR,
+                                                         16 * bi, n0, 0, 16 * bi);
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -329,8 +378,8 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
           }
         __syncwarp();
         zero(acc);
-        warp_mma<2, true, true, false>(acc, &sm.a[0][0], LDA, &rb[0][0], LDR, 16 * bi, n0,
-                                       16 * bi, 16 * bi + 16);
+        warp_mma<2, BF16X3, SPREAD, true, false, true>(acc, &sm.a[0][0], LDA, &rb[0][0], LDR,
+                                                       16 * bi, n0, 16 * bi, 16 * bi + 16);
         __syncwarp();
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
@@ -344,19 +393,20 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
     } else {
       const int m = warp - 4;
       zero(o1);
-      warp_mma<8, false, true, true>(o1, &sm.q[0][0], LDK, &sm.s[0][0], LDK, 16 * m, 0, 0, DK);
+      warp_mma<8, BF16X3, PAIR, true, true>(o1, &sm.q[0][0], LDK, &sm.s[0][0], LDK, 16 * m, 0, 0,
+                                            DK);
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o1[nt][e] *= sm.gam[16 * m + g + (e >> 1) * 8];
+        for (int e = 0; e < 4; ++e) o1[nt][e] *= sm.gam[16 * m + g + (e >> 1) * 8] * a.q_scale;
     }
     __syncthreads();  // W complete; S0 and Q no longer read
     if (c + 1 < n_chunks) issue_q(c + 1);
     if (warp >= 4) {
       // ---- O = diag(gamma) Q S0^T + P W -> global -------------------------------------------
       const int m = warp - 4;
-      warp_mma<8, false, true, false>(o1, &sm.p[0][0], LDA, &rb[0][0], LDR, 16 * m, 0, 0,
-                                      16 * m + 16);
+      warp_mma<8, BF16X3, SPREAD, true, false>(o1, &sm.p[0][0], LDA, &rb[0][0], LDR, 16 * m, 0, 0,
+                                               16 * m + 16);
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
@@ -374,8 +424,8 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
     {
       float acc[8][4];
       zero(acc);
-      warp_mma<8, true, false, false>(acc, &rb[0][0], LDR, &kb[0][0], LDK, 16 * mt,
-                                      64 * half, 0, C, sm.rdec);
+      warp_mma<8, BF16X3, SPREAD, false, false>(acc, &rb[0][0], LDR, &kb[0][0], LDK, 16 * mt,
+                                                64 * half, 0, C, sm.rdec);
       const float gc = sm.gam[C - 1];
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
