@@ -101,57 +101,66 @@ enum Fmt { F16, BF16, BF16X3 };
 // and for an [m|n][k] operand with row stride 4 mod 32.
 enum KOrder { PAIR, SPREAD };
 
-// acc[nt] (+)= A(m0.., k) B(k, n0 + 8 nt ..) over k in [k0, k1) (multiple of 16): one 16-row
-// tile, NT 8-col tiles.  A is [m][k] (AK) or [k][m]; B is [n][k] (BK) or [k][n]; ascale
-// (optional) scales A's column k.  SEP keeps the two BF16X3 correction products in their own
-// accumulators (shorter dependency chains for small NT).
-template <int NT, Fmt FMT, KOrder KO, bool AK, bool BK, bool SEP = false>
-__device__ __forceinline__ void warp_mma(float (&acc)[NT][4], const float* A, int lda,
-                                         const float* B, int ldb, int m0, int n0, int k0, int k1,
-                                         const float* ascale = nullptr) {
+// acc[i][nt] (+)= A(m0[i].., k) B(k, n0 + 8 nt ..) over k in [k0, k1) (a multiple of 16): MT
+// 16-row tiles sharing each B fragment, NT 8-col tiles of which the first nt_cnt are computed.
+// A is [m][k] (AK) or [k][m]; B is [n][k] (BK) or [k][n]; ascale (optional) scales A's column
+// k.  SEP keeps the two BF16X3 correction products in their own accumulators (shorter
+// dependency chains for small NT).
+template <int MT, int NT, Fmt FMT, KOrder KO, bool AK, bool BK, bool SEP = false>
+__device__ __forceinline__ void warp_mma_mt(float (&acc)[MT][NT][4], const float* A, int lda,
+                                            const int (&m0)[MT], const float* B, int ldb, int n0,
+                                            int k0, int k1, const float* ascale = nullptr,
+                                            int nt_cnt = NT) {
   static_assert(KO == SPREAD || (AK && BK), "PAIR order needs k-contiguous operands");
   const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   constexpr bool X3 = FMT == BF16X3;
-  float c1[X3 && SEP ? NT : 1][4], c2[X3 && SEP ? NT : 1][4];
+  constexpr int NC = X3 && SEP ? NT : 1;
+  float c1[MT][NC][4], c2[MT][NC][4];
 #pragma unroll
-  for (int i = 0; i < (X3 && SEP ? NT : 1); ++i)
+  for (int i = 0; i < MT; ++i)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) c1[i][e] = c2[i][e] = 0.f;
+    for (int j = 0; j < NC; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c1[i][j][e] = c2[i][j][e] = 0.f;
   // physical k of slots (2q, 2q+1, 2q+8, 2q+9)
   const int o0 = KO == PAIR ? 2 * q : q, o1 = KO == PAIR ? 2 * q + 1 : q + 4;
   const int o2 = o0 + 8, o3 = o1 + 8;
   for (int k = k0; k < k1; k += 16) {
-    float x[2][4];  // rows g, g + 8; slots 0..3
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int m = m0 + g + 8 * h;
-      if constexpr (KO == PAIR) {
-        const float2 r0 = *reinterpret_cast<const float2*>(A + m * lda + k + o0);
-        const float2 r1 = *reinterpret_cast<const float2*>(A + m * lda + k + o2);
-        x[h][0] = r0.x; x[h][1] = r0.y; x[h][2] = r1.x; x[h][3] = r1.y;
-      } else if constexpr (AK) {
-        x[h][0] = A[m * lda + k + o0]; x[h][1] = A[m * lda + k + o1];
-        x[h][2] = A[m * lda + k + o2]; x[h][3] = A[m * lda + k + o3];
-      } else {
-        x[h][0] = A[(k + o0) * lda + m]; x[h][1] = A[(k + o1) * lda + m];
-        x[h][2] = A[(k + o2) * lda + m]; x[h][3] = A[(k + o3) * lda + m];
-      }
-      if (ascale) {
-        x[h][0] *= ascale[k + o0]; x[h][1] *= ascale[k + o1];
-        x[h][2] *= ascale[k + o2]; x[h][3] *= ascale[k + o3];
-      }
-    }
     // a0 = row g slots 0,1; a1 = row g+8 slots 0,1; a2 = row g slots 2,3; a3 = row g+8 slots 2,3
-    uint32_t ah[4], al[4];
+    uint32_t ah[MT][4], al[MT][4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int h = r & 1, s0 = (r >> 1) * 2;
-      if constexpr (FMT == F16) ah[r] = pack_f16(x[h][s0], x[h][s0 + 1]);
-      else if constexpr (FMT == BF16) ah[r] = pack_bf16(x[h][s0], x[h][s0 + 1]);
-      else split_bf16(x[h][s0], x[h][s0 + 1], ah[r], al[r]);
+    for (int i = 0; i < MT; ++i) {
+      float x[2][4];  // rows g, g + 8; slots 0..3
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int m = m0[i] + g + 8 * h;
+        if constexpr (KO == PAIR) {
+          const float2 r0 = *reinterpret_cast<const float2*>(A + m * lda + k + o0);
+          const float2 r1 = *reinterpret_cast<const float2*>(A + m * lda + k + o2);
+          x[h][0] = r0.x; x[h][1] = r0.y; x[h][2] = r1.x; x[h][3] = r1.y;
+        } else if constexpr (AK) {
+          x[h][0] = A[m * lda + k + o0]; x[h][1] = A[m * lda + k + o1];
+          x[h][2] = A[m * lda + k + o2]; x[h][3] = A[m * lda + k + o3];
+        } else {
+          x[h][0] = A[(k + o0) * lda + m]; x[h][1] = A[(k + o1) * lda + m];
+          x[h][2] = A[(k + o2) * lda + m]; x[h][3] = A[(k + o3) * lda + m];
+        }
+        if (ascale) {
+          x[h][0] *= ascale[k + o0]; x[h][1] *= ascale[k + o1];
+          x[h][2] *= ascale[k + o2]; x[h][3] *= ascale[k + o3];
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int h = r & 1, s0 = (r >> 1) * 2;
+        if constexpr (FMT == F16) ah[i][r] = pack_f16(x[h][s0], x[h][s0 + 1]);
+        else if constexpr (FMT == BF16) ah[i][r] = pack_bf16(x[h][s0], x[h][s0 + 1]);
+        else split_bf16(x[h][s0], x[h][s0 + 1], ah[i][r], al[i][r]);
+      }
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
+      if (nt >= nt_cnt) break;
       const int n = n0 + 8 * nt + g;
       float y[4];
       if constexpr (KO == PAIR) {
@@ -166,29 +175,48 @@ __device__ __forceinline__ void warp_mma(float (&acc)[NT][4], const float* A, in
         y[2] = B[(k + o2) * ldb + n]; y[3] = B[(k + o3) * ldb + n];
       }
       if constexpr (FMT == F16) {
-        mma_f16(acc[nt], ah, pack_f16(y[0], y[1]), pack_f16(y[2], y[3]));
+        const uint32_t b0 = pack_f16(y[0], y[1]), b1 = pack_f16(y[2], y[3]);
+#pragma unroll
+        for (int i = 0; i < MT; ++i) mma_f16(acc[i][nt], ah[i], b0, b1);
       } else if constexpr (FMT == BF16) {
-        mma_bf16(acc[nt], ah, pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]));
+        const uint32_t b0 = pack_bf16(y[0], y[1]), b1 = pack_bf16(y[2], y[3]);
+#pragma unroll
+        for (int i = 0; i < MT; ++i) mma_bf16(acc[i][nt], ah[i], b0, b1);
       } else {
         uint32_t bh0, bl0, bh1, bl1;
         split_bf16(y[0], y[1], bh0, bl0);
         split_bf16(y[2], y[3], bh1, bl1);
-        if constexpr (SEP) {
-          mma_bf16(c1[nt], al, bh0, bh1);
-          mma_bf16(c2[nt], ah, bl0, bl1);
-        } else {
-          mma_bf16(acc[nt], al, bh0, bh1);
-          mma_bf16(acc[nt], ah, bl0, bl1);
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+          if constexpr (SEP) {
+            mma_bf16(c1[i][nt], al[i], bh0, bh1);
+            mma_bf16(c2[i][nt], ah[i], bl0, bl1);
+          } else {
+            mma_bf16(acc[i][nt], al[i], bh0, bh1);
+            mma_bf16(acc[i][nt], ah[i], bl0, bl1);
+          }
+          mma_bf16(acc[i][nt], ah[i], bh0, bh1);
         }
-        mma_bf16(acc[nt], ah, bh0, bh1);
       }
     }
   }
   if constexpr (X3 && SEP)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int i = 0; i < MT; ++i)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[nt][e] += c1[nt][e] + c2[nt][e];
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][nt][e] += c1[i][nt][e] + c2[i][nt][e];
+}
+
+// one 16-row tile
+template <int NT, Fmt FMT, KOrder KO, bool AK, bool BK, bool SEP = false>
+__device__ __forceinline__ void warp_mma(float (&acc)[NT][4], const float* A, int lda,
+                                         const float* B, int ldb, int m0, int n0, int k0, int k1,
+                                         const float* ascale = nullptr, int nt_cnt = NT) {
+  const int mm[1] = {m0};
+  warp_mma_mt<1, NT, FMT, KO, AK, BK, SEP>(reinterpret_cast<float(&)[1][NT][4]>(acc), A, lda,
+                                           mm, B, ldb, n0, k0, k1, ascale, nt_cnt);
 }
 
 template <int NT>
@@ -303,22 +331,44 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
       sm.rdec[2 * lane + 1] = expf(LC - s);
     }
     __syncthreads();
-    // ---- G = K K^T -> A;  RHS = beta (V - diag(gamma) K S0^T) over the V rows --------------
+    // ---- lower triangles of G = K K^T (warps 0-3, -> A) and Q K^T (warps 4-7, -> P) ---------
+    // Only the 16x16 blocks on or below the diagonal are used: 20 8-column tiles per product,
+    // dealt 5 to each warp as units (m-tile, first n-tile, count): warp u of a group takes
+    // (3, 0, 5) | (3, 5, 3) + (0, 0, 2) | (2, 0, 5) | (2, 5, 1) + (1, 0, 4).
+    {
+      const int u = warp & 3;
+      const bool is_g = warp < 4;
+      const float* Aop = is_g ? &kb[0][0] : &sm.q[0][0];
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        const int m = v == 0 ? (u < 2 ? 3 : 2) : (u == 1 ? 0 : 1);
+        const int nt0 = v == 0 && (u & 1) ? 5 : 0;
+        const int cnt = v == 0 ? ((u & 1) ? (u == 1 ? 3 : 1) : 5) : (u == 1 ? 2 : (u == 3 ? 4 : 0));
+        if (cnt == 0) continue;
+        float acc[5][4];
+        zero(acc);
+        warp_mma<5, F16, PAIR, true, true>(acc, Aop, LDK, &kb[0][0], LDK, 16 * m, 8 * nt0, 0, DK,
+                                           nullptr, cnt);
+#pragma unroll
+        for (int nt = 0; nt < 5; ++nt) {
+          if (nt >= cnt) break;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = 16 * m + g + (e >> 1) * 8, i = 8 * (nt0 + nt) + 2 * qd + (e & 1);
+            if (is_g)
+              sm.a[t][i] = i < t ? sm.beta[t] * expf(sm.L[t] - sm.L[i]) * acc[nt][e] : 0.f;
+            else
+              sm.p[t][i] = i <= t ? expf(sm.L[t] - sm.L[i]) * (acc[nt][e] * a.q_scale) : 0.f;
+          }
+        }
+      }
+    }
+    // ---- RHS = beta (V - diag(gamma) K S0^T) over the V rows, warp (mt, half): 16 x 32 -------
     {
       float acc[4][4];
       zero(acc);
-      warp_mma<4, F16, PAIR, true, true>(acc, &kb[0][0], LDK, &kb[0][0], LDK, 16 * mt,
-                                     32 * half, 0, DK);
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = 16 * mt + g + (e >> 1) * 8, i = 32 * half + 8 * nt + 2 * qd + (e & 1);
-          sm.a[t][i] = i < t ? sm.beta[t] * expf(sm.L[t] - sm.L[i]) * acc[nt][e] : 0.f;
-        }
-      zero(acc);
       warp_mma<4, BF16, PAIR, true, true>(acc, &kb[0][0], LDK, &sm.s[0][0], LDK, 16 * mt,
-                                     32 * half, 0, DK);
+                                          32 * half, 0, DK);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
@@ -328,6 +378,11 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
         }
     }
     __syncthreads();
+    // warps 4-7: q_scale diag(gamma) Q S0^T on the m-tile pair {pm, 3 - pm} (equal shares of the
+    // triangular P W below), columns 32 ch .. 32 ch + 31; kept in registers across the sync
+    const int pm = (warp >> 1) & 1, ch = warp & 1;
+    const int mm[2] = {16 * pm, 16 * (3 - pm)};
+    float o1[2][4][4];
     if (warp < 4) {
       // ---- diagonal 16x16 block `warp` of T = (I + A)^-1 in place; lane j = column j -------
       // Right-looking forward substitution: once x[r] is final it updates every later row, so
@@ -344,23 +399,7 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
       if (lane < 16)
 #pragma unroll
         for (int r = 0; r < 16; ++r) sm.a[o + r][o + j] = col[r];
-    } else {
-      // ---- meanwhile P = M o Q K^T, one 16-row tile per warp ------------------------------------
-      const int m = warp - 4;
-      float acc[8][4];
-      zero(acc);
-      warp_mma<8, F16, PAIR, true, true>(acc, &sm.q[0][0], LDK, &kb[0][0], LDK, 16 * m, 0, 0, DK);
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = 16 * m + g + (e >> 1) * 8, i = 8 * nt + 2 * qd + (e & 1);
-          sm.p[t][i] = i <= t ? expf(sm.L[t] - sm.L[i]) * (acc[nt][e] * a.q_scale) : 0.f;
-        }
-    }
-    __syncthreads();
-    float o1[8][4];  // warps 4-7: diag(gamma) Q S0^T of their 16-row tile, kept across the sync
-    if (warp < 4) {
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 0-3: all four blocks inverted
       // ---- W = (I + A)^-1 RHS by blocked forward substitution, warp w owning 16 columns ------
       const int n0 = 16 * warp;
       for (int bi = 0; bi < 4; ++bi) {
@@ -391,36 +430,40 @@ __global__ void __launch_bounds__(dnc::THREADS, 1)
         __syncwarp();
       }
     } else {
-      const int m = warp - 4;
-      zero(o1);
-      warp_mma<8, BF16X3, PAIR, true, true>(o1, &sm.q[0][0], LDK, &sm.s[0][0], LDK, 16 * m, 0, 0,
-                                            DK);
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+      for (int i = 0; i < 2; ++i) zero(o1[i]);
+      warp_mma_mt<2, 4, BF16X3, PAIR, true, true>(o1, &sm.q[0][0], LDK, mm, &sm.s[0][0], LDK,
+                                                  32 * ch, 0, DK);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o1[nt][e] *= sm.gam[16 * m + g + (e >> 1) * 8] * a.q_scale;
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o1[i][nt][e] *= sm.gam[mm[i] + g + (e >> 1) * 8] * a.q_scale;
     }
     __syncthreads();  // W complete; S0 and Q no longer read
     if (c + 1 < n_chunks) issue_q(c + 1);
     if (warp >= 4) {
-      // ---- O = diag(gamma) Q S0^T + P W -> global -------------------------------------------
-      const int m = warp - 4;
-      warp_mma<8, BF16X3, SPREAD, true, false>(o1, &sm.p[0][0], LDA, &rb[0][0], LDR, 16 * m, 0, 0,
-                                               16 * m + 16);
+      // ---- O = q_scale diag(gamma) Q S0^T + P W -> global ----------------------------------
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+      for (int i = 0; i < 2; ++i) {
+        warp_mma<4, BF16X3, SPREAD, true, false>(o1[i], &sm.p[0][0], LDA, &rb[0][0], LDR, mm[i],
+                                                 32 * ch, 0, mm[i] + 16);
 #pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          const int t = t0 + 16 * m + g + (e >> 1) * 8, j = 8 * nt + 2 * qd;
-          if (t < a.n_tok) {
-            bad |= !isfinite(o1[nt][e]) || !isfinite(o1[nt][e + 1]);
-            *reinterpret_cast<float2*>(a.o + (size_t)b * a.o_bs + (size_t)t * a.o_ts +
-                                       (size_t)h * a.dv + sl * DS + j) =
-                make_float2(o1[nt][e], o1[nt][e + 1]);
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; e += 2) {
+            const int t = t0 + mm[i] + g + (e >> 1) * 8, j = 32 * ch + 8 * nt + 2 * qd;
+            if (t < a.n_tok) {
+              bad |= !isfinite(o1[i][nt][e]) || !isfinite(o1[i][nt][e + 1]);
+              *reinterpret_cast<float2*>(a.o + (size_t)b * a.o_bs + (size_t)t * a.o_ts +
+                                         (size_t)h * a.dv + sl * DS + j) =
+                  make_float2(o1[i][nt][e], o1[i][nt][e + 1]);
+            }
           }
-        }
+      }
     }
-    // ---- S = gamma_C S0 + W^T diag(exp(L_C - L)) K  (3xTF32), warp w: its 16 x 64 share -------
+    // ---- S = gamma_C S0 + W^T diag(exp(L_C - L)) K  (BF16X3), warp w: its 16 x 64 share ------
     {
       float acc[8][4];
       zero(acc);
