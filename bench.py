@@ -678,7 +678,7 @@ def run_dnet_prefill(args, world, rank, local):
                      "peak_kind": peak_kind + " (sustained bf16)",
                      "flop_per_launch": 2 * mac,
                      "note": "FLOPs of the chunked (WY, C=64) algorithm, which the kernel "
-                             "runs on mma.sync TF32 (3xTF32 for the solve and state update)"},
+                             "runs on mma.sync m16n8k16 (f16, bf16 and hi/lo-split bf16)"},
         "gpu_launches": 3 * K, "clocks": sampler.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

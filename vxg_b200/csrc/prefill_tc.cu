@@ -191,7 +191,6 @@ __global__ void __launch_bounds__(pftc::THREADS, 1)
   }
   const int key_end = min(len, base + t0 + QT);
   const int n_tiles = (key_end + KT - 1) / KT;
-  const int nb = HD / 32;
 
   if (tid == 0) {
     for (int i = 0; i < NRAW; ++i) {
