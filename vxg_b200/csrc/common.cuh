@@ -32,6 +32,18 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---- programmatic dependent launch -------------------------------------------------------------
+// A kernel launched with programmatic stream serialisation may start while the previous kernel
+// of its stream still runs; before it reads that kernel's results it waits for the previous
+// grid to complete and its memory to be visible.  The previous kernel lets it start early by
+// triggering.  Both are no-ops for kernels launched the ordinary way.
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- mbarrier + 1-D bulk async copy (TMA engine, no tensor map, local source) ---------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

@@ -21,6 +21,7 @@
 #include "kernels.h"
 
 #include <algorithm>
+#include <utility>
 
 namespace vxg {
 
@@ -298,6 +299,7 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
   const int kh = warp & 1, sub = (warp >> 1) % SPK, grp = warp / WPS;
   const int slot_sub = warp >> 1;  // grp * SPK + sub
   const int B = a.n_batch;
+  grid_dep_trigger();  // the combine pass may be scheduled as this grid's CTAs retire
 
   // ---- unit prefix over the batch (warp 0: serial per lane chunk + warp scan) -----------
   if (warp == 0) {
@@ -336,6 +338,9 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
     fence_mbar_init();
   }
   __syncthreads();
+  // The unit prefix only reads the step's inputs; the cache (and the partial slots the previous
+  // combine read) only after the kernel before this one -- the append -- has completed.
+  grid_dep_wait();
   const long long U = sm.prefix[B];
   const int u0 = (int)((long long)blockIdx.x * U / gridDim.x);
   const int u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
@@ -676,6 +681,8 @@ __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partial
   using namespace fast;
   constexpr int H = NKV * G;
   constexpr int MAXS = 512 * SUBS;  // every split CTA may meet the entry (grid <= 512)
+  grid_dep_wait();  // the split pass's partials and published ranges
+  grid_dep_trigger();
   const int b = blockIdx.x, z = blockIdx.z;
   const int tid = threadIdx.x, dl = tid % kCombineDims, sl = tid / kCombineDims;
   const int d = blockIdx.y * kCombineDims + dl;
@@ -825,6 +832,7 @@ __global__ void __launch_bounds__(256) decode_fast_combine_final(DecodeArgs a, P
                                                                  float* l_out, float* o_out) {
   using namespace fast;
   constexpr int H = NKV * G;
+  grid_dep_wait();  // the slot-split combine's intermediates
   const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const float* im = part.inter;
   const float* il = im + (size_t)a.n_batch * S * H;
@@ -961,17 +969,35 @@ Partials carve_partials(float* base, const DecodeArgs& a, int sm_count) {
 }
 
 namespace {
+// Launch with programmatic stream serialisation: the kernel may start before the previous
+// kernel of the stream completes and waits for it (grid_dep_wait) before using its results.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 cudaError_t launch_fast_combine(const DecodeArgs& a, const Partials& part, int sm_count,
                                 const float* gate, float* out, float* m_out, float* l_out,
                                 float* o_out, cudaStream_t st) {
   const int S = combine_splits(a);
-  decode_fast_combine<<<dim3(a.n_batch, fast::HD / kCombineDims, S), 256, 0, st>>>(
-      a, part, fast_grid(sm_count), S, gate, out, m_out, l_out, o_out);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_dependent(decode_fast_combine,
+                                   dim3(a.n_batch, fast::HD / kCombineDims, S), dim3(256), 0, st,
+                                   a, part, fast_grid(sm_count), S, gate, out, m_out, l_out,
+                                   o_out);
   if (e != cudaSuccess || S == 1) return e;
-  decode_fast_combine_final<<<dim3(a.n_batch, fast::NKV * fast::G), fast::HD, 0, st>>>(
-      a, part, S, gate, out, m_out, l_out, o_out);
-  return cudaGetLastError();
+  return launch_dependent(decode_fast_combine_final, dim3(a.n_batch, fast::NKV * fast::G),
+                          dim3(fast::HD), 0, st, a, part, S, gate, out, m_out, l_out, o_out);
 }
 }  // namespace
 
@@ -990,8 +1016,8 @@ static cudaError_t run_split(const DecodeArgs& a, const Partials& p, int sm_coun
     }
     *mode = 1;
     *max_split = 0;
-    decode_fast_split<<<fast_grid(sm_count), fast::THREADS, sizeof(fast::Smem), st>>>(a, p);
-    return cudaGetLastError();
+    return launch_dependent(decode_fast_split, dim3(fast_grid(sm_count)), dim3(fast::THREADS),
+                            sizeof(fast::Smem), st, a, p);
   }
   *mode = 0;
   *max_split = generic_max_split(a);

@@ -26,6 +26,7 @@ __global__ void __launch_bounds__(256) q8_append_kernel(const int32_t* __restric
                                                          int n_batch, int n_tok, int n_seq,
                                                          int cap, int n_kv, int nb,
                                                          uint32_t* status) {
+  grid_dep_trigger();  // a decode pass launched after this may start its set-up now
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int per_tok = n_kv * nb;                 // blocks per token in one cache
