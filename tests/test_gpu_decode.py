@@ -171,6 +171,45 @@ def test_device_tensors_and_torch_stream(ctx):
     np.testing.assert_array_equal(dev.cpu().numpy(), host)
 
 
+def test_decode_steps_replayed_from_cuda_graph(ctx):
+    """Append + attend steps captured once in a CUDA graph and replayed give the eager results
+    (the append, split and combine kernels of a step are chained by programmatic dependent
+    launch, which a capture must keep in order)."""
+    import torch
+    rng = np.random.default_rng(29)
+    lens = [700, 2100, 64]
+    pool, kh, vh, cap = make_pool(ctx, rng, lens, 2, 256, cap=2200)
+    n, steps = len(lens), 3
+    seq = torch.arange(n, dtype=torch.int32, device="cuda")
+    pos = [torch.tensor(lens, dtype=torch.int32, device="cuda") + i for i in range(steps)]
+    q = [torch.from_numpy(rng.standard_normal((n, 16, 256)).astype(np.float32)).cuda()
+         for _ in range(steps)]
+    kn = [torch.from_numpy(rng.standard_normal((n, 2, 256)).astype(np.float32)).cuda()
+          for _ in range(steps)]
+    vn = [torch.from_numpy(rng.standard_normal((n, 2, 256)).astype(np.float32)).cuda()
+          for _ in range(steps)]
+    outs = [torch.empty((n, 16, 256), device="cuda") for _ in range(steps)]
+    for i in range(steps):
+        pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=outs[i], max_ctx=cap)
+    torch.cuda.synchronize()
+    eager = [o.cpu().numpy().copy() for o in outs]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(steps):
+            # the appends rewrite the same positions with the same K/V on every replay
+            pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=outs[i], max_ctx=cap)
+    for rep in range(2):
+        for o in outs:
+            o.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        for i in range(steps):
+            np.testing.assert_allclose(outs[i].cpu().numpy(), eager[i], atol=ATOL, rtol=RTOL,
+                                       err_msg=f"replay {rep} step {i}")
+    del g
+    assert ctx.sync() == 0
+
+
 def test_nonfinite_query_reports_warning(ctx):
     rng = np.random.default_rng(27)
     pool, kh, vh, cap = make_pool(ctx, rng, [50], 2, 256)
