@@ -969,24 +969,6 @@ Partials carve_partials(float* base, const DecodeArgs& a, int sm_count) {
 }
 
 namespace {
-// Launch with programmatic stream serialisation: the kernel may start before the previous
-// kernel of the stream completes and waits for it (grid_dep_wait) before using its results.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                             cudaStream_t st, Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
 cudaError_t launch_fast_combine(const DecodeArgs& a, const Partials& part, int sm_count,
                                 const float* gate, float* out, float* m_out, float* l_out,
                                 float* o_out, cudaStream_t st) {

@@ -183,11 +183,13 @@ __global__ void __launch_bounds__(256, 1) deltanet_step_persistent(DeltaNetArgs 
   const int tid = threadIdx.x, rip = tid / LPR, sl = tid % LPR;
   const int n_items = a.n_batch * a.n_vh;
   const uint32_t st_bytes = (uint32_t)a.dv * DK * 4;
+  grid_dep_trigger();  // the next step's kernel may be scheduled as these CTAs retire
   if (tid == 0) {
     for (int i = 0; i < dn::NS; ++i) mbar_init(&sm.full[i], 1);
     fence_mbar_init();
   }
   __syncthreads();
+  grid_dep_wait();  // every input (the state above all) only after the previous kernel is done
   auto issue = [&](int item, int buf) {
     const int b = item / a.n_vh, h = item - b * a.n_vh;
     const int hk = h / (a.n_vh / a.n_kh);
@@ -523,11 +525,13 @@ cudaError_t launch_deltanet_step(const DeltaNetArgs& a, cudaStream_t st) {
     }
     const int items = a.n_batch * a.n_vh;
     const unsigned grid = (unsigned)std::min(items, sms);
+    // chained to the previous kernel of the stream (typically the previous step, whose state it
+    // reads): its CTAs are set up as that kernel's CTAs retire
     if (a.dk == 128)
-      deltanet_step_persistent<128><<<grid, 256, sizeof(dn::Smem), st>>>(a);
-    else
-      deltanet_step_persistent<64><<<grid, 256, sizeof(dn::Smem), st>>>(a);
-    return cudaGetLastError();
+      return launch_dependent(deltanet_step_persistent<128>, dim3(grid), dim3(256),
+                              sizeof(dn::Smem), st, a);
+    return launch_dependent(deltanet_step_persistent<64>, dim3(grid), dim3(256), sizeof(dn::Smem),
+                            st, a);
   }
   const unsigned grid = (unsigned)a.n_batch * a.n_vh;
   switch (a.dk) {

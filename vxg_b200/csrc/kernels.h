@@ -1,8 +1,29 @@
 // Internal launch interface between the C-ABI host layer (abi.cu) and the kernels.
 #pragma once
+#include <utility>
+
 #include "common.cuh"
 
 namespace vxg {
+
+// Launch with programmatic stream serialisation: the kernel may start before the previous
+// kernel of the stream completes; it must call grid_dep_wait() before it reads anything that
+// kernel wrote (and before it reads anything written earlier in the stream).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // q8_append.cu -----------------------------------------------------------------------------
 // For batch entry b and token t < n_tok: quantise k_new/v_new[b][t][n_kv][32*nb] into
