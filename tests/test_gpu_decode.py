@@ -210,6 +210,35 @@ def test_decode_steps_replayed_from_cuda_graph(ctx):
     assert ctx.sync() == 0
 
 
+def test_back_to_back_calls_on_gpu_computed_positions(ctx):
+    """Decode calls issued back to back on one stream, each right after a torch kernel that
+    computes its positions, without append: every call sees its own positions and the previous
+    call's combine is done with the shared scratch before the next split reuses it."""
+    import torch
+    rng = np.random.default_rng(31)
+    lens = [1500, 333, 2900, 64, 777]
+    pool, kh, vh, cap = make_pool(ctx, rng, lens, 2, 256, cap=3000)
+    n, calls = len(lens), 5
+    seq_np = np.arange(n, dtype=np.int32)
+    qs = rng.standard_normal((calls, n, 16, 256)).astype(np.float32)
+    seq = torch.from_numpy(seq_np).cuda()
+    p = torch.tensor(lens, dtype=torch.int32, device="cuda") - 1
+    q_dev = torch.from_numpy(qs).cuda()
+    torch.cuda.synchronize()
+    outs = []
+    for i in range(calls):
+        p = p - 3 * (i + 1)  # a kernel on the same stream right before the call
+        outs.append(pool.decode(seq, p, q_dev[i]))
+    torch.cuda.synchronize()
+    assert ctx.sync() == 0
+    pos = np.array(lens, np.int32) - 1
+    for i in range(calls):
+        pos = pos - 3 * (i + 1)
+        want = pool.decode(seq_np, pos, qs[i])
+        np.testing.assert_allclose(outs[i].cpu().numpy(), want, atol=ATOL, rtol=RTOL,
+                                   err_msg=f"call {i}")
+
+
 def test_nonfinite_query_reports_warning(ctx):
     rng = np.random.default_rng(27)
     pool, kh, vh, cap = make_pool(ctx, rng, [50], 2, 256)

@@ -300,6 +300,10 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
   const int slot_sub = warp >> 1;  // grp * SPK + sub
   const int B = a.n_batch;
   grid_dep_trigger();  // the combine pass may be scheduled as this grid's CTAs retire
+  // Launched to overlap the previous kernel's tail: everything it reads or writes in global
+  // memory (positions, cache, partial slots and the published ranges a previous combine may
+  // still be reading) waits until that kernel has completed.
+  grid_dep_wait();
 
   // ---- unit prefix over the batch (warp 0: serial per lane chunk + warp scan) -----------
   if (warp == 0) {
@@ -338,9 +342,6 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
     fence_mbar_init();
   }
   __syncthreads();
-  // The unit prefix only reads the step's inputs; the cache (and the partial slots the previous
-  // combine read) only after the kernel before this one -- the append -- has completed.
-  grid_dep_wait();
   const long long U = sm.prefix[B];
   const int u0 = (int)((long long)blockIdx.x * U / gridDim.x);
   const int u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
