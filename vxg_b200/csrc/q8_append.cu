@@ -6,16 +6,36 @@
 // with the reference: IEEE division for amax/127 and 1/df (no fast-math), binary16 RNE for the
 // scale, round-half-even for the codes, NaN -> 0 like Rust's saturating `as i8`.
 //
-// One warp quantises one 32-value block: lane i owns value i, the block max is a warp
-// reduction, lane i writes code byte i and lane 0 writes the 2-byte scale.
+// Eight lanes quantise one 32-value block, four values each: the block max is a reduction
+// over the 8-lane group, each lane writes its four code bytes (two 16-bit stores; records are
+// 34 bytes, 2-byte aligned) and the group's first lane the 2-byte scale.  A warp covers four
+// consecutive blocks, so loads and stores of neighbouring warps are contiguous.
 #include "kernels.h"
 
 namespace vxg {
 
-__device__ __forceinline__ float load_f32(const float* p) { return *p; }
-__device__ __forceinline__ float load_f32(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void load4(const float* p, bool vec, float (&x)[4]) {
+  if (vec) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = p[i];
+  }
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, bool vec, float (&x)[4]) {
+  if (vec) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    x[0] = __uint_as_float(v.x << 16); x[1] = __uint_as_float(v.x & 0xFFFF0000u);
+    x[2] = __uint_as_float(v.y << 16); x[3] = __uint_as_float(v.y & 0xFFFF0000u);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(p[i]);
+  }
+}
 
 // T = float or __nv_bfloat16 (bf16 widens to f32 exactly, so the codes are those of the f32 value)
+// vec: k_new / v_new allow 16-byte (f32) or 8-byte (bf16) loads of four values.
 template <typename T>
 __global__ void __launch_bounds__(256) q8_append_kernel(const int32_t* __restrict__ seq_ids,
                                                          const int32_t* __restrict__ pos,
@@ -24,50 +44,67 @@ __global__ void __launch_bounds__(256) q8_append_kernel(const int32_t* __restric
                                                          uint8_t* __restrict__ k_pool,
                                                          uint8_t* __restrict__ v_pool,
                                                          int n_batch, int n_tok, int n_seq,
-                                                         int cap, int n_kv, int nb,
+                                                         int cap, int n_kv, int nb, bool vec,
                                                          uint32_t* status) {
   grid_dep_trigger();  // a decode pass launched after this may start its set-up now
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  const long long blk_id = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+  const int sub = threadIdx.x & 7;
   const int per_tok = n_kv * nb;                 // blocks per token in one cache
   const long long per_cache = (long long)n_batch * n_tok * per_tok;
-  if (warp >= 2 * per_cache) return;
-  const int which = warp >= per_cache;            // 0 = K, 1 = V
-  const long long r = warp - which * per_cache;
-  const int bt = (int)(r / per_tok);              // (batch, token) index
-  const int blk = (int)(r - (long long)bt * per_tok);
+  // every lane takes part in the group reduction; lanes past the end or on a bad index carry 0
+  bool ok = blk_id < 2 * per_cache;
+  const int which = ok && blk_id >= per_cache;   // 0 = K, 1 = V
+  const long long r = blk_id - which * per_cache;
+  const int bt = ok ? (int)(r / per_tok) : 0;    // (batch, token) index
+  const int blk = ok ? (int)(r - (long long)bt * per_tok) : 0;
   const int b = bt / n_tok;
   const int t = bt - b * n_tok;
-  const int s = seq_ids[b];
-  const int p = pos[b] + t;
-  if (s < 0 || s >= n_seq || p < 0 || p >= cap) {
-    if (lane == 0) atomicOr(status, kStatusBadIndex);
-    return;
+  int s = 0, p = 0;
+  if (ok) {
+    s = seq_ids[b];
+    p = pos[b] + t;
+    if (s < 0 || s >= n_seq || p < 0 || p >= cap) {
+      if (sub == 0) atomicOr(status, kStatusBadIndex);
+      ok = false;
+    }
   }
-  const T* src = (which ? v_new : k_new) + ((size_t)bt * per_tok + blk) * 32;
-  const float x = load_f32(src + lane);
+  float x[4] = {0.f, 0.f, 0.f, 0.f};
+  if (ok) load4((which ? v_new : k_new) + ((size_t)bt * per_tok + blk) * 32 + 4 * sub, vec, x);
   // amax starts at 0 and ignores NaN (f32::max); fmaxf(0, NaN) = 0 gives the same.
-  const float amax = warp_max(fmaxf(0.0f, fabsf(x)));
-  const uint16_t dh = f32_to_f16bits(amax / 127.0f);
+  float m = fmaxf(fmaxf(0.0f, fabsf(x[0])), fmaxf(0.0f, fabsf(x[1])));
+  m = fmaxf(m, fmaxf(fmaxf(0.0f, fabsf(x[2])), fmaxf(0.0f, fabsf(x[3]))));
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (!ok) return;
+  const uint16_t dh = f32_to_f16bits(m / 127.0f);
   const float df = f16bits_to_f32(dh);
   const float inv = df > 0.0f ? 1.0f / df : 0.0f;
-  const float rq = rintf(x * inv);
-  const int qi = (rq == rq) ? (int)fminf(fmaxf(rq, -127.0f), 127.0f) : 0;
+  uint32_t code[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float rq = rintf(x[i] * inv);
+    const int qi = (rq == rq) ? (int)fminf(fmaxf(rq, -127.0f), 127.0f) : 0;
+    code[i] = (uint32_t)qi & 0xFFu;
+  }
   uint8_t* dst = (which ? v_pool : k_pool) + (((size_t)s * cap + p) * per_tok + blk) * kBlk;
-  dst[2 + lane] = (uint8_t)(int8_t)qi;
-  if (lane == 0) *reinterpret_cast<uint16_t*>(dst) = dh;
+  uint16_t* d16 = reinterpret_cast<uint16_t*>(dst + 2 + 4 * sub);
+  d16[0] = (uint16_t)(code[0] | (code[1] << 8));
+  d16[1] = (uint16_t)(code[2] | (code[3] << 8));
+  if (sub == 0) *reinterpret_cast<uint16_t*>(dst) = dh;
 }
 
 cudaError_t launch_q8_append(const int32_t* seq_ids, const int32_t* pos, const float* k_new,
                              const float* v_new, uint8_t* k_pool, uint8_t* v_pool, int n_batch,
                              int n_tok, int n_seq, int cap, int n_kv, int nb, uint32_t* status,
                              cudaStream_t stream) {
-  const long long warps = 2LL * n_batch * n_tok * n_kv * nb;
-  if (warps == 0) return cudaSuccess;
+  const long long n_blk = 2LL * n_batch * n_tok * n_kv * nb;
+  if (n_blk == 0) return cudaSuccess;
   const int threads = 256;
-  const long long blocks = (warps * 32 + threads - 1) / threads;
+  const long long blocks = (n_blk * 8 + threads - 1) / threads;
+  const bool vec = ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15u) == 0;
   q8_append_kernel<float><<<(unsigned)blocks, threads, 0, stream>>>(
-      seq_ids, pos, k_new, v_new, k_pool, v_pool, n_batch, n_tok, n_seq, cap, n_kv, nb, status);
+      seq_ids, pos, k_new, v_new, k_pool, v_pool, n_batch, n_tok, n_seq, cap, n_kv, nb, vec,
+      status);
   return cudaGetLastError();
 }
 
@@ -75,14 +112,15 @@ cudaError_t launch_q8_append_bf16(const int32_t* seq_ids, const int32_t* pos, co
                                   const void* v_new, uint8_t* k_pool, uint8_t* v_pool, int n_batch,
                                   int n_tok, int n_seq, int cap, int n_kv, int nb, uint32_t* status,
                                   cudaStream_t stream) {
-  const long long warps = 2LL * n_batch * n_tok * n_kv * nb;
-  if (warps == 0) return cudaSuccess;
+  const long long n_blk = 2LL * n_batch * n_tok * n_kv * nb;
+  if (n_blk == 0) return cudaSuccess;
   const int threads = 256;
-  const long long blocks = (warps * 32 + threads - 1) / threads;
+  const long long blocks = (n_blk * 8 + threads - 1) / threads;
+  const bool vec = ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 7u) == 0;
   q8_append_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, stream>>>(
       seq_ids, pos, static_cast<const __nv_bfloat16*>(k_new),
       static_cast<const __nv_bfloat16*>(v_new), k_pool, v_pool, n_batch, n_tok, n_seq, cap, n_kv,
-      nb, status);
+      nb, vec, status);
   return cudaGetLastError();
 }
 
