@@ -31,6 +31,13 @@ def test_library_exports_every_declared_symbol():
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
 
 
+def test_integration_guide_binds_every_declared_symbol():
+    """INTEGRATION.md's Rust extern blocks declare every entry point of the header."""
+    guide = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    missing = [n for n in header_symbols() if f"fn {n}(" not in guide]
+    assert not missing, missing
+
+
 def test_version():
     assert b"sm_100a" in _lib.lib().vxg_attn_cuda_version()
 
