@@ -56,7 +56,7 @@ extern "C" {
 #define VXG_ATTN_MEM_HOST 0
 #define VXG_ATTN_MEM_DEVICE 1
 
-/* Library version string. */
+/* Library version string (as vxg_version_string, include/vxg.h:40). */
 VXG_ATTN_API const char* vxg_attn_cuda_version(void);
 
 /* ---------------------------------------------------------------- context ------------------ */
@@ -66,20 +66,22 @@ VXG_ATTN_API void* vxg_attn_cuda_create(char* err, size_t cap);
 /* Synchronises and frees the context (native/cuda.cu:68). */
 VXG_ATTN_API void vxg_attn_cuda_destroy(void* ctx);
 /* Waits for all work on `stream` (NULL: the context stream), then reports the device status
- * word: VXG_ATTN_WARN_NONFINITE, VXG_ATTN_ERR_INVALID_OPTION for skipped out-of-range entries,
+ * word (no counterpart: the reference's CUDA calls return only when done, native/cuda.cu:43-66): VXG_ATTN_WARN_NONFINITE, VXG_ATTN_ERR_INVALID_OPTION for skipped out-of-range entries,
  * VXG_ATTN_ERR_INTERNAL for a device error or a bounded wait that gave up. */
 VXG_ATTN_API int vxg_attn_cuda_sync(void* ctx, void* stream, char* err, size_t cap);
-/* Number of SMs of the bound device (the split-KV grid size). */
+/* Number of SMs of the bound device (the split-KV grid size).  No counterpart in the reference. */
 VXG_ATTN_API int vxg_attn_cuda_sm_count(void* ctx);
 /* Device time in ms of the last split-KV attention pass launched on the context (when timing
  * is enabled with vxg_attn_cuda_set_timing); -1 if unavailable.  Like the reference's
  * kernel_ms out-parameter (native/cuda.cu:52-60). */
 VXG_ATTN_API int vxg_attn_cuda_set_timing(void* ctx, int enable);
 VXG_ATTN_API double vxg_attn_cuda_last_split_ms(void* ctx);
-/* Test hook: 1 forces the portable split kernel for every shape (cross-check of the fast one). */
+/* Test hook: 1 forces the portable split kernel for every shape (cross-check of the fast one).
+ * No counterpart in the reference. */
 VXG_ATTN_API int vxg_attn_cuda_force_generic(void* ctx, int enable);
 
-/* Device / pinned memory for callers without a CUDA toolchain (Rust, C). */
+/* Device / pinned memory for callers without a CUDA toolchain (Rust, C).  No counterpart in the
+ * reference, whose CUDA codec allocates inside each call (native/cuda.cu:43-66). */
 VXG_ATTN_API void* vxg_attn_cuda_malloc(void* ctx, size_t bytes, char* err, size_t cap);
 VXG_ATTN_API void vxg_attn_cuda_free(void* ctx, void* dptr);
 VXG_ATTN_API void* vxg_attn_cuda_host_alloc(void* ctx, size_t bytes, char* err, size_t cap);
@@ -95,14 +97,18 @@ VXG_ATTN_API int vxg_attn_cuda_memcpy(void* ctx, void* dst, const void* src, siz
  * multiple of 32 (llm.rs:291) and at most 256. */
 VXG_ATTN_API void* vxg_attn_cuda_kv_create(void* ctx, uint32_t n_seq, uint32_t n_head_kv, uint32_t head_dim,
                               uint32_t cap_tokens, char* err, size_t cap);
+/* Frees the pools (vxt_metal_cb4_fast_state_destroy, metal_cb4_fast_ffi.rs:156). */
 VXG_ATTN_API void vxg_attn_cuda_kv_destroy(void* kv);
 /* Bytes held by the K and V pools (metal_cb4_fast_ffi.rs:157, llm.rs:340-346). */
 VXG_ATTN_API size_t vxg_attn_cuda_kv_bytes(void* kv);
+/* Tokens per sequence the pools hold now (grown by vxg_attn_cuda_kv_reserve).  No counterpart:
+ * the reference's Vec<KvQ8Block> grows implicitly (llm_prefill.rs:311-324). */
 VXG_ATTN_API uint32_t vxg_attn_cuda_kv_capacity(void* kv);
 /* Grows every sequence to at least cap_tokens tokens, keeping contents (doubling policy of
  * native/metal_cb4_fast.h:174-191). */
 VXG_ATTN_API int vxg_attn_cuda_kv_reserve(void* kv, uint32_t cap_tokens, char* err, size_t cap);
-/* Device base pointers of the K and V pools and the byte stride between sequences. */
+/* Device base pointers of the K and V pools and the byte stride between sequences (for
+ * vxg_attn_cuda_q8_decode_noalloc and callers' own kernels).  No counterpart in the reference. */
 VXG_ATTN_API int vxg_attn_cuda_kv_device_ptrs(void* kv, void** k_pool, void** v_pool, size_t* seq_stride);
 /* Byte-identical import / export of tokens [tok_begin, tok_begin + n_tok) of sequence `seq`:
  * k_blocks / v_blocks are n_tok * n_head_kv * head_dim/32 KvQ8Blocks (34 B each), i.e. a slice
@@ -164,7 +170,8 @@ VXG_ATTN_API int vxg_attn_cuda_q8_decode(void* ctx, void* kv, uint32_t n_batch, 
  * step t to be back on the host.  Inputs are read, and `out` written, asynchronously: keep the
  * input buffers unchanged and do not read `out` until vxg_attn_cuda_ticket_wait has returned for
  * the ticket.  Pinned host memory (vxg_attn_cuda_host_alloc) is required for the copies to
- * overlap. */
+ * overlap.  (The Metal runner's asynchronous pair vxt_metal_cb4_fast_enqueue_async / _wait_cmd,
+ * metal_cb4_fast_ffi.rs:194-204, is the nearest shape.) */
 VXG_ATTN_API int vxg_attn_cuda_q8_decode_host_async(void* ctx, void* kv, uint32_t n_batch,
                             uint32_t n_head, const int32_t* seq_ids, const int32_t* pos,
                             const float* q, const float* k_new, const float* v_new,
@@ -236,7 +243,8 @@ VXG_ATTN_API int vxg_attn_cuda_q8_prefill(void* ctx, void* kv, uint32_t n_batch,
  * (b, head) the running max m (log2 units: max_t score_t * log2(e)), the sum
  * l = sum_t 2^(score_t*log2(e) - m) and the unnormalised o = sum_t 2^(...) * v_t.  Shapes:
  * m, l [n_batch][n_head]; o [n_batch][n_head][head_dim].  Empty ranges give m = -inf, l = 0,
- * o = 0.  This is the per-GPU half of the multi-GPU KV-range split. */
+ * o = 0.  This is the per-GPU half of the multi-GPU KV-range split; no counterpart in the
+ * reference (one device), its softmax (llm_prefill.rs:347-362) re-associated over token ranges. */
 VXG_ATTN_API int vxg_attn_cuda_q8_decode_partial(void* ctx, void* kv, uint32_t n_batch, uint32_t n_head,
                                     const int32_t* seq_ids, const int32_t* kv_begin,
                                     const int32_t* kv_end, const float* q, float scale,
@@ -244,7 +252,9 @@ VXG_ATTN_API int vxg_attn_cuda_q8_decode_partial(void* ctx, void* kv, uint32_t n
                                     void* stream, char* err, size_t cap);
 
 /* Log-sum-exp merge of n_parts partials (layout [n_parts][n_rows] for m and l,
- * [n_parts][n_rows][head_dim] for o) into out [n_rows][head_dim]; optional sigmoid gate. */
+ * [n_parts][n_rows][head_dim] for o) into out [n_rows][head_dim]; optional sigmoid gate
+ * (llm_prefill.rs:363-368).  The other half of the KV-range split; no counterpart in the
+ * reference. */
 VXG_ATTN_API int vxg_attn_cuda_lse_combine(void* ctx, uint32_t n_parts, uint32_t n_rows, uint32_t head_dim,
                               const float* m, const float* l, const float* o, const float* gate,
                               float* out, int memkind, void* stream, char* err, size_t cap);
