@@ -189,11 +189,16 @@ VXG_ATTN_API int vxg_attn_cuda_ticket_wait(void* ctx, uint64_t ticket, char* err
  * that must not stall on cudaMalloc, which can synchronise the device.  It allocates nothing:
  * every argument is caller-owned device memory, the KV pools included (layout as above, e.g.
  * from vxg_attn_cuda_kv_device_ptrs or the caller's own buffers), and its split-KV scratch is a
- * built-in 16 MiB device array that each GPU using the library keeps until the process exits.
+ * built-in 32 MiB device array that each GPU using the library keeps until the process exits.
  * A batch whose scratch does not fit is rejected with VXG_ATTN_ERR_BUFFER_TOO_SMALL (at 16 q /
- * 2 kv heads, head_dim 256 on a 148-SM B200: up to 106 entries per call).  All calls on a device
- * share that array, so calls that overlap on the GPU race; serialise them.  The first call on a
- * device sets up the array's address for that device; make it before any stream capture.  With
+ * 2 kv heads, head_dim 256 on a 148-SM B200: up to 190 entries per call; fewer on GPUs with more
+ * SMs).  Other shapes run the generic split kernel, whose scratch grows with cap_tokens, so there
+ * the batch limit falls as the pools' capacity grows (63 entries at 16 q heads, head_dim 128
+ * and a 32768-token pool).  All calls on a device share that array, so calls that overlap on
+ * the GPU race; serialise them.  The first call on a device sets up the array's address for that
+ * device; make it before any stream capture.  That address is kept per device index for the
+ * device's primary context (the CUDA runtime's default); do not call this from a second,
+ * driver-API context on the same device.  With
  * stream == NULL the call runs on the default stream and reports the device status like
  * vxg_attn_cuda_q8_decode; with a stream it is asynchronous and reports launch errors only. */
 VXG_ATTN_API int vxg_attn_cuda_q8_decode_noalloc(

@@ -64,12 +64,71 @@ def test_noalloc_matches_allocating_entry_point(n_head, n_kv, hd):
     ctx.close()
 
 
+SCRATCH_BYTES = 32 << 20      # the built-in array, less the 256-byte status word below
+STATUS_BYTES = 256
+
+
+def _scratch_bytes_16_2_256(n, sm_count):
+    """Split-KV scratch of one call at 16 q / 2 kv heads, head_dim 256 (the fast kernel): six
+    (m, l, o) slots per (CTA, entry) boundary, a second level of slots when the combine splits
+    a small batch, and the unit prefix plus CTA ranges."""
+    grid = min(sm_count, 512)
+    floats = (grid + n) * 6 * 16 * 258
+    splits = max(1, min(32, -(-128 // (4 * n))))
+    if splits > 1:
+        floats += n * splits * 16 * 258
+    return 4 * (floats + n + grid + 64)
+
+
+def _largest_batch(sm_count):
+    n = 1
+    while _scratch_bytes_16_2_256(n + 1, sm_count) + STATUS_BYTES <= SCRATCH_BYTES:
+        n += 1
+    return n
+
+
+def test_noalloc_batch_limit_boundary():
+    """The largest batch that fits the array runs and matches the allocating entry point; one
+    entry more is rejected before anything is launched."""
+    import torch
+    torch.cuda.set_device(0)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    n = _largest_batch(sms)
+    assert n >= 64, f"a 64-sequence batch should fit on {sms} SMs"
+    rng = np.random.default_rng(71)
+    n_seq, L = 8, 300
+    ctx = vxg_b200.Context()
+    pool = vxg_b200.KvQ8Pool(ctx, n_seq, 2, 256, L)
+    for s in range(n_seq):
+        kb = oracle.q8_quantize(rng.standard_normal((L, 2, 256)).astype(np.float32))
+        vb = oracle.q8_quantize(rng.standard_normal((L, 2, 256)).astype(np.float32))
+        pool.import_blocks(s, 0, kb, vb)
+    seq = (np.arange(n) % n_seq).astype(np.int32)
+    pos = rng.integers(0, L, n).astype(np.int32)
+    q = rng.standard_normal((n, 16, 256)).astype(np.float32)
+    want = pool.decode(seq, pos, q)
+    out = torch.full((n, 16, 256), float("nan"), device="cuda")
+    rc, msg = _noalloc(pool, torch.from_numpy(seq).cuda(), torch.from_numpy(pos).cuda(),
+                       torch.from_numpy(q).cuda(), out, 16)
+    assert rc == 0, msg
+    np.testing.assert_allclose(out.cpu().numpy(), want, atol=ATOL, rtol=RTOL)
+    m = n + 1
+    seq1 = torch.zeros(m, dtype=torch.int32, device="cuda")
+    out1 = torch.zeros((m, 16, 256), device="cuda")
+    rc, msg = _noalloc(pool, seq1, seq1.clone(), torch.zeros((m, 16, 256), device="cuda"), out1,
+                       16)
+    assert rc == _lib.ERR_BUFFER_TOO_SMALL and "scratch" in msg
+    assert not out1.any()                       # rejected before any launch
+    pool.close()
+    ctx.close()
+
+
 def test_noalloc_rejects_batches_beyond_its_scratch():
     import torch
     torch.cuda.set_device(0)
     ctx = vxg_b200.Context()
     pool = vxg_b200.KvQ8Pool(ctx, 1, 2, 256, 16)
-    n = 400                                     # > 106 entries at this shape
+    n = 400                                     # well past the limit at this shape
     seq = torch.zeros(n, dtype=torch.int32, device="cuda")
     pos = torch.zeros(n, dtype=torch.int32, device="cuda")
     q = torch.zeros((n, 16, 256), device="cuda")

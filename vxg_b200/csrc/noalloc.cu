@@ -9,9 +9,13 @@
 // this library holds until the process exits.
 //
 // Limits and sharing:
-//  * the array is kScratchBytes (16 MiB); a call whose partials do not fit is rejected with
+//  * the array is kScratchBytes (32 MiB); a call whose partials do not fit is rejected with
 //    VXG_ATTN_ERR_BUFFER_TOO_SMALL before anything is launched.  At 16 query / 2 KV heads,
-//    head_dim 256 on a 148-SM B200 that is up to 106 batch entries per call;
+//    head_dim 256 the partials take ((SMs + n) * 6 * 16 * 258 + n + SMs + 64) floats for n >= 32
+//    entries (a little more below 32, where the combine splits slots), so a 148-SM B200 takes up
+//    to 190 batch entries per call.  Other shapes run the generic split kernel, whose partials
+//    grow with cap_tokens (n * ceil(cap_tokens / 512) * n_head * (head_dim + 2) floats): there
+//    the batch limit shrinks as the pools' capacity grows;
 //  * every call on a device uses the same array, so calls that overlap on the GPU (different
 //    streams, or several host threads) race and must be serialised by the caller;
 //  * each call clears the status word it needs; the partials are fully written by a call before
@@ -19,7 +23,10 @@
 //
 // The first call on a device does a one-time set-up with that device current: it looks up the
 // array's device address with cudaGetSymbolAddress (host code cannot use the array's name as a
-// device address) and the SM count.  Make that first call before any stream capture.
+// device address) and the SM count.  Make that first call before any stream capture.  The
+// address is cached per device index, which assumes every call on a device runs in that
+// device's primary context (the CUDA runtime's default); a caller that makes its own driver-API
+// contexts must not call this entry point from more than one context per device.
 #include "vxg_attn_cuda.h"
 #include "kernels.h"
 
@@ -29,7 +36,7 @@
 
 namespace {
 
-constexpr size_t kScratchBytes = size_t(16) << 20;
+constexpr size_t kScratchBytes = size_t(32) << 20;
 constexpr size_t kStatusBytes = 256;  // the status word, padded to keep the partials aligned
 constexpr int kMaxDevices = 64;
 
@@ -104,9 +111,14 @@ extern "C" int vxg_attn_cuda_q8_decode_noalloc(
   if (n_batch == 0) return VXG_ATTN_OK;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+  if (e != cudaSuccess) {
     put(err, cap, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
     return VXG_ATTN_ERR_INTERNAL;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    put(err, cap, "device index " + std::to_string(dev) + " is beyond the " +
+                      std::to_string(kMaxDevices) + " devices this entry point keeps set-up for");
+    return VXG_ATTN_ERR_UNSUPPORTED;
   }
   DeviceScratch ds;
   int rc = setup(dev, &ds, err, cap);
