@@ -83,3 +83,53 @@ def test_import_export_roundtrip_and_reserve(ctx):
     assert np.array_equal(k3, kb) and np.array_equal(v3, vb)
     z, _ = pool.export_blocks(1, 20, 5)
     assert not z.any()
+
+
+def _amax_for_scale(x):
+    """A float32 block maximum m with fl32(m / 127) == x, so the quantiser's scale rounding sees
+    exactly x (the reference's f32_to_f16(amax / 127), llm_prefill.rs:30-31)."""
+    a = np.float32(x) * np.float32(127)
+    for _ in range(8):
+        for cand in (a, np.nextafter(a, np.float32(np.inf)), np.nextafter(a, np.float32(0))):
+            if np.float32(cand) / np.float32(127) == np.float32(x):
+                return np.float32(cand)
+        a = np.nextafter(a, np.float32(0))
+    return None
+
+
+def test_append_scale_rounding_on_reference_f16_cases(ctx):
+    """The reference's f16 known-answer cases (fp16.rs:89-108) run through the GPU quantiser:
+    one block per case whose amax / 127 is that case's f32 value, so the block scale passes
+    through every subnormal and half-ULP boundary of the test.  The scale bits written by the
+    GPU must equal the reference's expected f16 bits, and the whole block must equal the
+    oracle's bytes."""
+    import json
+    import os
+    kat = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "fp16_kat.json")))
+    rng = np.random.default_rng(14)
+    blocks, expect = [], []
+    for c in kat["cases"]:
+        x = np.array([c["f32_bits"]], np.uint32).view(np.float32)[0]
+        if not np.isfinite(x) or np.signbit(x):
+            continue                      # a block scale is |max| / 127: finite, non-negative
+        m = _amax_for_scale(x)
+        if m is None or not np.isfinite(m):
+            continue
+        blk = (rng.uniform(-1, 1, 32) * m * np.float32(0.99)).astype(np.float32)
+        blk[rng.integers(32)] = m if rng.random() < 0.5 else -m
+        blocks.append(blk)
+        expect.append(c["f16_bits"])
+    assert len(blocks) >= 8
+    n_kv, hd = 2, 256
+    per_tok = n_kv * hd // 32
+    T = -(-len(blocks) // per_tok)
+    flat = np.zeros((T * per_tok, 32), np.float32)
+    flat[:len(blocks)] = np.stack(blocks)
+    toks = flat.reshape(T, n_kv, hd)
+    pool = vxg_b200.KvQ8Pool(ctx, 1, n_kv, hd, T)
+    pool.append(np.zeros(1, np.int32), np.zeros(1, np.int32), toks[None], toks[None], n_tok=T)
+    kb, vb = pool.export_blocks(0, 0, T)
+    assert np.array_equal(kb, oracle.q8_quantize(toks))
+    assert np.array_equal(vb, kb)
+    d = kb.reshape(-1, 34)[:len(blocks), :2].copy().view(np.uint16)[:, 0]
+    assert d.tolist() == expect
