@@ -31,11 +31,15 @@ def test_library_exports_every_declared_symbol():
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
 
 
-def test_integration_guide_binds_every_declared_symbol():
-    """INTEGRATION.md's Rust extern blocks declare every entry point of the header."""
-    guide = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    missing = [n for n in header_symbols() if f"fn {n}(" not in guide]
+def test_rust_binding_declares_every_declared_symbol():
+    """The committed Rust binding (include/vxg_attn_cuda.rs) declares every entry point of the
+    header, each once, and nothing the header does not declare."""
+    rs = open(os.path.join(ROOT, "include", "vxg_attn_cuda.rs")).read()
+    missing = [n for n in header_symbols() if f"fn {n}(" not in rs]
     assert not missing, missing
+    declared = re.findall(r"\bfn (vxg_attn_cuda_\w+)\(", rs)
+    assert len(declared) == len(set(declared)), "an entry point is declared twice"
+    assert set(declared) <= set(header_symbols()), set(declared) - set(header_symbols())
 
 
 def test_version():

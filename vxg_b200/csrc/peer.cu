@@ -8,9 +8,10 @@
 // A step is two launches on the caller's stream.  peer_push_kernel (one CTA) stores this rank's
 // packed partials into slot `rank` of every rank's buffer (its own included) with plain stores
 // through the IPC mappings, fences at system scope, then raises flag[p][rank] = step in every
-// buffer.  peer_combine_kernel (one CTA per row) waits, bounded in wall-clock time, until all
-// `world` flags of its own buffer show the step, then merges the parts with the log-sum-exp
-// combine of lse_combine_kernel.  The step counter lives in device memory, so a CUDA graph of
+// buffer with a system-scope release store.  peer_combine_kernel (one CTA per row) waits,
+// bounded in wall-clock time, until all `world` flags of its own buffer show the step
+// (system-scope acquire loads), then merges the parts with the log-sum-exp combine of
+// lse_combine_kernel.  The step counter lives in device memory, so a CUDA graph of
 // steps replays correctly.  Parity double-buffering makes the reuse of a slot safe: a rank
 // pushes step s + 2 only after its combine of step s + 1, which needed every rank's push of
 // step s + 1, which each rank issued after its own combine of step s.
@@ -28,8 +29,15 @@ __device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
   asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_volatile(uint32_t* p, uint32_t v) {
-  asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// The step flags are written with release and read with acquire semantics at system scope:
+// a reader that sees a flag also sees the partials stored before it, on whichever GPU.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 }  // namespace
 
@@ -57,11 +65,11 @@ __global__ void __launch_bounds__(512) peer_push_kernel(const float* __restrict_
     }
   }
   __threadfence_system();  // this thread's stores reach every GPU before the flags below
-  __syncthreads();
+  __syncthreads();         // ... and every thread's stores precede thread 0's releases
   if (threadIdx.x == 0) {
     for (int d = 0; d < world; ++d) {
       uint32_t* flags = reinterpret_cast<uint32_t*>(peers.buf[d] + (size_t)2 * world * per);
-      st_volatile(flags + p * world + rank, step);
+      st_release_sys(flags + p * world + rank, step);
     }
     *local_step = step;
   }
@@ -81,7 +89,7 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(const float* buf, int
     int ok = 1;
     uint64_t t0 = 0;
     for (int r = 0; r < world && ok; ++r) {
-      for (uint32_t i = 0; ld_volatile(flags + p * world + r) != step; ++i) {
+      for (uint32_t i = 0; ld_acquire_sys(flags + p * world + r) != step; ++i) {
         if ((i & 1023u) == 0) {
           uint64_t t;
           asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -93,8 +101,7 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(const float* buf, int
         }
       }
     }
-    __threadfence();  // the parts are read after their flags
-    s_ok = ok;
+    s_ok = ok;  // the acquiring loads above order the reads of the parts (after the barrier)
     s_step = step;
   }
   __syncthreads();

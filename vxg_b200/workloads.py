@@ -33,10 +33,13 @@ class DecodeBatch:
         return int(((self.ctx_lens().astype(np.int64) + step + 1) * TOKEN_BYTES).sum())
 
 
-def fill_pool_device(pool, ctx_lens, seed: int, outlier_frac: float = 0.0, chunk: int = 8192):
+def fill_pool_device(pool, ctx_lens, seed: int, outlier_frac: float = 0.0, chunk: int = 8192,
+                     offset: int = 0):
     """Fill sequence s of ``pool`` with ctx_lens[s] tokens of N(0,1) K/V (device RNG), quantised
-    by the library's append kernel.  With outlier_frac, that fraction of (token, kv head) K rows
-    is scaled x8 before quantisation."""
+    by the library's append kernel, at positions [offset, offset + ctx_lens[s]).  With
+    outlier_frac, that fraction of (token, kv head) K rows is scaled x8 before quantisation.
+    The tokens depend only on the seed and the lengths, not on the offset, so one rank's slice
+    of a split sequence can be rebuilt inside a whole-sequence pool."""
     import torch
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
@@ -50,7 +53,7 @@ def fill_pool_device(pool, ctx_lens, seed: int, outlier_frac: float = 0.0, chunk
                 m = torch.rand((1, n, pool.n_head_kv, 1), generator=g, device="cuda") < outlier_frac
                 k = torch.where(m, k * 8.0, k)
             seq = torch.tensor([s], dtype=torch.int32, device="cuda")
-            pos = torch.tensor([t0], dtype=torch.int32, device="cuda")
+            pos = torch.tensor([t0 + offset], dtype=torch.int32, device="cuda")
             pool.append(seq, pos, k.contiguous(), v.contiguous(), n_tok=n)
     pool.ctx.sync()
 
