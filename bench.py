@@ -5,8 +5,11 @@ Default workload: per GPU, 64 sequences with context lengths
 (seeded), 16 query / 2 KV heads, head_dim 256, Q8_0 KV.  One step = quantise-and-append one new
 N(0,1) K/V token per sequence, then split-KV attention of each sequence's query over its whole
 cache.  Inputs are synthetic (device RNG; see vxg_b200/workloads.py).  Multi-GPU: one process
-per GPU, each with its own 64 sequences (weak scaling, no data-path collective); time = max over
-ranks of the device-timed region.
+per GPU, each with its own 64 sequences of the same context lengths (weak scaling, no data-path
+collective); time = max over ranks of the device-timed region.  After the config-2 line is
+measured, the same run times config 3 (one 262144-token context: split-KV over the SMs on one
+GPU, KV-range split with an exchange of the (m, l, o) partials on N GPUs) and reports it under
+"long_context" (--no-long skips it).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload decode|long|deltanet|prefill|dnet_prefill]
@@ -142,6 +145,14 @@ def barrier_max(torch, dist, world, value: float) -> float:
     return float(t.item())
 
 
+def barrier_min(torch, dist, world, value: float) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return float(t.item())
+
+
 def barrier(torch, dist, world):
     if world > 1:
         dist.barrier()
@@ -157,7 +168,9 @@ def run_decode(args, world, rank, local):
 
     K, W = args.steps, args.warmup
     ctx = vxg_b200.Context()
-    batch = wl.DecodeBatch(n_seq=args.seqs, ctx_hi=args.ctx_max, seed=1 + 1000 * rank)
+    # every rank decodes the same context lengths (its own K/V data and queries), so the
+    # max-over-ranks step time measures the GPUs, not a per-rank workload imbalance
+    batch = wl.DecodeBatch(n_seq=args.seqs, ctx_hi=args.ctx_max, seed=1)
     lens = batch.ctx_lens()
     n = batch.n_seq
     E2E_W = 2
@@ -232,7 +245,8 @@ def run_decode(args, world, rank, local):
     q_bytes = n * wl.HQ * wl.HD * 4
     alg_bytes = kv_bytes + q_bytes
     peak, peak_kind = measured_peaks()
-    achieved = alg_bytes / (split_ms_max * 1e-3) / 1e9
+    # each rank's own bytes over its own split time; the slowest rank's figure is reported
+    achieved = barrier_min(torch, dist, world, alg_bytes / (split_ms * 1e-3) / 1e9)
     step_bytes = alg_bytes + n * (wl.HQ * wl.HD * 4 + 2 * wl.HKV * wl.HD * 4 + 1088)
 
     res = {
@@ -270,17 +284,36 @@ def run_decode(args, world, rank, local):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_decode(pool, lens, n)
+    pool.close()
+    del q, kn, vn
+    torch.cuda.empty_cache()
+    if not args.no_long:
+        # config 3 on the same GPUs (one GPU: split-KV over its SMs; N GPUs: KV-range split)
+        barrier(torch, dist, world)
+        lr = measure_long(args, world, rank, local, ctx, K, W, check=world > 1)
+        pool_l = lr.pop("_pool", None)
+        lr.pop("_inputs", None)
+        if pool_l is not None:
+            pool_l.close()
+        res["long_context"] = lr
     return res
 
 
-def cpu_baseline_decode(pool, lens, n, budget_s=12.0, n_sample=8):
-    """The oracle port on this host's cores over a bounded sample: n_sample of the sequences
-    (their real caches, exported from the device), one append+attend step each, repeated until
-    ~budget_s of wall time."""
+def cpu_sample_size(n, cores):
+    """Sequences per CPU step: one per host thread (at least 4, at most the batch), so every
+    thread of the oracle has a sequence; the reference arm uses the same first sequences."""
+    return int(min(n, max(4, cores)))
+
+
+def cpu_baseline_decode(pool, lens, n, budget_s=12.0):
+    """The oracle port on this host's cores over a bounded sample: the first
+    cpu_sample_size() sequences of the batch (their real caches, exported from the device), one
+    append+attend step each, repeated until ~budget_s of wall time."""
     from oracle import oracle
     from vxg_b200 import workloads as wl
     rng = np.random.default_rng(99)
-    pick = np.sort(rng.choice(n, n_sample, replace=False))
+    n_sample = cpu_sample_size(n, host_cores())
+    pick = np.arange(n_sample)
     cap = int(lens[pick].max()) + 2
     kpool = np.zeros((n_sample, cap, wl.HKV, wl.HD // 32, 34), np.uint8)
     vpool = np.zeros_like(kpool)
@@ -305,8 +338,9 @@ def cpu_baseline_decode(pool, lens, n, budget_s=12.0, n_sample=8):
         if el >= budget_s or reps >= 1000:
             break
     return {"value": n_sample * reps / el, "unit": "seq-steps/s", "cores": cores, "kind": "port",
-            "sample": f"{n_sample} of the 64 sequences (mean ctx {lens[pick].mean():.0f}), one "
-                      f"append+attend step each, x{reps} repetitions, {el:.1f} s"}
+            "sample": f"the first {n_sample} of the 64 sequences (mean ctx "
+                      f"{lens[pick].mean():.0f}), one append+attend step each, {cores} threads, "
+                      f"x{reps} repetitions, {el:.1f} s"}
 
 
 def _timed_reps(fn, budget_s, max_reps=1000):
@@ -462,25 +496,26 @@ def run_deltanet(args, world, rank, local):
     return res
 
 
-def run_long(args, world, rank, local):
+def measure_long(args, world, rank, local, ctx, K, W, check=False):
     """B=1, ctx 262144, 1% of K rows x8.  One GPU: split-KV across its SMs.
     N GPUs: the KV range is split across ranks (vxg_b200.dist.LongContextDecoder): append on the
-    owning rank, per-rank split-KV partial, NCCL all-gather of (m, l, o), LSE combine.  A step
-    is ~0.1 ms of device work, so on N GPUs the K timed steps (Python step + NCCL call) are
-    captured once into a CUDA graph and replayed; the split time per launch comes from an eager
-    pass of K further steps."""
+    owning rank, per-rank split-KV partial, exchange of (m, l, o) (NVLink peer memory or one
+    NCCL all-gather), LSE combine.  A step is ~0.1 ms of device work, so on N GPUs the K timed
+    steps are captured once into a CUDA graph and replayed; the split time per launch comes from
+    an eager pass of K further steps.  With ``check``, the first step's merged output is compared
+    on rank 0 with a one-GPU decode of the same whole cache, before anything is timed."""
     import torch
     import torch.distributed as dist
     import vxg_b200
     from vxg_b200 import workloads as wl
-    K, W = args.steps, args.warmup
-    ctx = vxg_b200.Context()
     L = 262144
-    n_in = W + 2 * K
+    n_in = 1 + W + 2 * K
     cap = L + n_in + 8
     q, kn, vn = wl.decode_step_inputs_device(1, n_in, seed=4)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    dec = pool = None
+    check_err = None
     if world == 1:
         pool = vxg_b200.KvQ8Pool(ctx, 1, wl.HKV, wl.HD, cap)
         wl.fill_pool_device(pool, [L], seed=3, outlier_frac=0.01)
@@ -489,30 +524,51 @@ def run_long(args, world, rank, local):
         out = torch.empty((1, wl.HQ, wl.HD), device="cuda")
         step = lambda i: pool.decode(seq, pos[i], q[i], kn[i], vn[i], out=out, max_ctx=cap)
     else:
-        from vxg_b200.dist import LongContextDecoder
+        from vxg_b200.dist import KvRange, LongContextDecoder
         dec = LongContextDecoder(ctx, cap, wl.HQ, wl.HKV, wl.HD, world, rank,
                                  exchange=args.exchange)
         mine = dec.range.local_len(L)
         wl.fill_pool_device(dec.pool, [mine], seed=3 + rank, outlier_frac=0.01)
         step = lambda i: dec.step(L + i, q[i], kn[i], vn[i])
-    for i in range(W):
+        if check:
+            got = step(0).clone()
+            torch.cuda.synchronize()
+            if rank == 0:
+                # the whole sequence on this GPU alone: every rank's slice rebuilt from its seed
+                full = vxg_b200.KvQ8Pool(ctx, 1, wl.HKV, wl.HD, L + 1)
+                for r in range(world):
+                    kr = KvRange(cap, world, r)
+                    wl.fill_pool_device(full, [kr.local_len(L)], seed=3 + r, outlier_frac=0.01,
+                                        offset=kr.begin)
+                one = full.decode(torch.zeros(1, dtype=torch.int32, device="cuda"),
+                                  torch.tensor([L], dtype=torch.int32, device="cuda"), q[0],
+                                  kn[0], vn[0], max_ctx=L + 1)
+                check_err = float((one[0] - got.reshape(one[0].shape)).abs().max())
+                full.close()
+                del one
+            barrier(torch, dist, world)
+    first = 1 if (world > 1 and check) else 0
+    for i in range(first, first + W):
         step(i)
     ctx.sync()
+    t0 = first + W
     graph = None
     if world > 1:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            for i in range(W, W + K):
+            for i in range(t0, t0 + K):
                 step(i)
         graph.replay()
         torch.cuda.synchronize()
     # split-pass timing (events between the kernels) on steps of their own, before the timed ones
     barrier(torch, dist, world)
     ctx.set_timing(True)
-    for i in range(W + K, W + 2 * K):
+    n_split = min(n_in, t0 + 2 * K) - (t0 + K)
+    for i in range(t0 + K, t0 + K + n_split):
         step(i)
     torch.cuda.synchronize()
-    split = barrier_max(torch, dist, world, ctx.split_ms_total() / K)
+    split_local = ctx.split_ms_total() / max(1, n_split)
+    split = barrier_max(torch, dist, world, split_local)
     ctx.set_timing(False)
     barrier(torch, dist, world)
     sampler = ClockSampler(local)
@@ -521,37 +577,70 @@ def run_long(args, world, rank, local):
     if graph is not None:
         graph.replay()
     else:
-        for i in range(W, W + K):
+        for i in range(t0, t0 + K):
             step(i)
     e1.record()
     torch.cuda.synchronize()
     sampler.stop()
+    rc = ctx.sync()
     ms = barrier_max(torch, dist, world, e0.elapsed_time(e1))
     del graph
     torch.cuda.synchronize()
-    if world > 1:
+    # algorithmic bytes of this rank's split launches: its own share of the mean context
+    mean_ctx = L + t0 + K // 2
+    alg = float((mean_ctx if dec is None else dec.range.local_len(mean_ctx)) * wl.TOKEN_BYTES)
+    if dec is not None:
         dec.close()
-    alg = (L + W + K / 2) * wl.TOKEN_BYTES / world
+        dec.pool.close()
     peak, peak_kind = measured_peaks()
-    ach = alg / (split * 1e-3) / 1e9
-    res = {"metric": METRIC, "value": K / (ms * 1e-3), "unit": "seq-steps/s", "n_gpus": world,
-            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config3: B=1 ctx 262144, 1% K rows x8, split-KV over SMs"
-                                   + (f" and {world} GPUs ("
-                                      + ("partials through NVLink peer memory, "
-                                         if args.exchange == "peer" else "NCCL all-gather, ")
-                                      + "LSE combine, CUDA graph of the K steps)"
-                                      if world > 1 else ""),
-                       "l2": "inputs larger than L2 (285 MB of KV per step)"},
-            "roofline": {"kernel": "decode_fast_split", "bound": "hbm", "achieved": ach,
-                         "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                         "peak_kind": peak_kind, "split_ms_per_launch": split},
-            "gpu_launches": (3 if world == 1 else 4) * K, "clocks": sampler.summary()}
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        i = W + 2 * K - 1
-        res["cpu_baseline"] = cpu_baseline_long(pool, L + W + K, q[i].cpu().numpy(),
-                                                kn[i].cpu().numpy(), vn[i].cpu().numpy())
+    ach = barrier_min(torch, dist, world, alg / (split_local * 1e-3) / 1e9)
+    res = {"workload": "config3: B=1 ctx 262144, 1% K rows x8, split-KV over SMs"
+                       + (f" and {world} GPUs (KV-range split, partials "
+                          + ("through NVLink peer memory" if args.exchange == "peer"
+                             else "by one NCCL all-gather")
+                          + ", LSE combine, CUDA graph of the K steps)" if world > 1 else ""),
+           "value": K / (ms * 1e-3), "unit": "seq-steps/s", "scaling": "strong",
+           "ms_per_step": ms / K, "split_ms_per_launch": split,
+           "exchange_and_merge_ms": max(0.0, ms / K - split),
+           "exchange": (args.exchange if world > 1 else "none (one GPU)"),
+           "roofline": {"kernel": "decode_fast_split", "bound": "hbm", "achieved": ach,
+                        "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                        "peak_kind": peak_kind, "note": "slowest rank: its own bytes over its "
+                        "own split time", "algorithmic_bytes_per_launch": alg},
+           "gpu_launches": (3 if world == 1 else 4) * K, "clocks": sampler.summary(),
+           "device_status": rc}
+    if check_err is not None:
+        res["check_vs_one_gpu_max_abs_err"] = check_err
+    if pool is not None:
+        res["_pool"] = pool
+        res["_inputs"] = (L + t0 + K, q[n_in - 1], kn[n_in - 1], vn[n_in - 1])
+    return res
+
+
+def run_long(args, world, rank, local):
+    """BASELINE config 3 as the main line (``--workload long``)."""
+    import vxg_b200
+    ctx = vxg_b200.Context()
+    K, W = args.steps, args.warmup
+    lr = measure_long(args, world, rank, local, ctx, K, W, check=world > 1)
+    pool = lr.pop("_pool", None)
+    inputs = lr.pop("_inputs", None)
+    res = {"metric": METRIC, "value": lr["value"], "unit": "seq-steps/s", "n_gpus": world,
+           "steps": K, "warmup": W, "ms_per_step": lr["ms_per_step"], "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": lr["workload"],
+                      "l2": "inputs larger than L2 (285 MB of KV per step)"},
+           "roofline": dict(lr["roofline"], split_ms_per_launch=lr["split_ms_per_launch"]),
+           "long_context": {k: v for k, v in lr.items()
+                            if k in ("exchange", "exchange_and_merge_ms",
+                                     "check_vs_one_gpu_max_abs_err")},
+           "gpu_launches": lr["gpu_launches"], "clocks": lr["clocks"]}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and pool is not None:
+        L, qi, ki, vi = inputs
+        res["cpu_baseline"] = cpu_baseline_long(pool, L, qi.cpu().numpy(), ki.cpu().numpy(),
+                                                vi.cpu().numpy())
+    if pool is not None:
+        pool.close()
     return res
 
 
@@ -700,7 +789,7 @@ def run_reference(args, world, rank):
     cores = host_cores()
     batch = wl.DecodeBatch(seed=1)
     lens = batch.ctx_lens()
-    S = int(min(batch.n_seq, max(4, cores)))
+    S = cpu_sample_size(batch.n_seq, cores)
     lens = lens[:S]
     rng = np.random.default_rng(17)
     cap = int(lens.max()) + W + K + 1
@@ -754,6 +843,8 @@ def main():
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "long", "deltanet", "prefill", "dnet_prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-long", action="store_true",
+                    help="decode workload: skip the config-3 long-context leg")
     ap.add_argument("--seqs", type=int, default=64, help="sequences per GPU (profiling runs)")
     ap.add_argument("--ctx-max", type=int, default=32768, help="context upper bound (profiling)")
     ap.add_argument("--prompts", type=int, default=8, help="prefill prompts per GPU (profiling)")
