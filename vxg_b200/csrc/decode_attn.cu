@@ -10,17 +10,19 @@
 //
 // Two split kernels feed one combine kernel:
 //  * decode_fast_split  -- head_dim 256, 8 query heads per kv head, 2 kv heads (the Qwen3.5
-//    full-attention shape).  Persistent: one CTA per SM takes an equal share of all
-//    64-token units of the batch, so ragged contexts load-balance to within one unit.  Raw
-//    34-byte blocks are staged with 1-D bulk async copies (3-deep ring, mbarrier completion),
-//    QK^T runs on int8 tensor cores (m16n8k32; the q vector is split into two int8 digits,
-//    the K codes feed the MMA unchanged), PV runs on f16 tensor cores (m16n8k16; codes
-//    widened exactly to f16, the per-token V scale folded into P).
+//    full-attention shape).  Persistent: one CTA per SM (12 warps) takes an equal share of
+//    all 96-token units of the batch, so ragged contexts load-balance to within one unit.
+//    Raw 34-byte blocks are staged with 1-D bulk async copies (2-deep ring of 96-token
+//    stages, mbarrier completion), QK^T runs on int8 tensor cores (m16n8k32; the q vector is
+//    split into two int8 digits, three for heads with outlier channels; the K codes feed the
+//    MMA unchanged), PV runs on f16 tensor cores (m16n8k16; codes widened exactly to f16, the
+//    per-token V scale folded into P, which the three-digit path also splits into f16 hi/lo).
 //  * decode_generic_split -- any n_head / n_kv / head_dim (multiple of 32): FFMA, one warp per
 //    token, warp reductions.  Used for every other shape and as a cross-check.
 #include "kernels.h"
 
 #include <algorithm>
+#include <type_traits>
 #include <utility>
 
 namespace vxg {
@@ -166,6 +168,11 @@ constexpr int THREADS = WARPS * 32;
 constexpr int SUBS = SPK * GROUPS; // partial slots per (CTA, batch entry) per kv head
 constexpr int MAXB = 1024;         // batch entries per launch
 constexpr uint64_t kWaitNs = 2000000000ull;  // give up a stage wait after 2 s
+// Largest max|q| * scale of a warp's 8 query heads that the two-digit query split serves: its
+// error per q element is max|q| / (2 * 127 * 254), so below this bound the score error stays
+// far inside the output tolerance (N(0,1) queries at head_dim 256 sit near 0.25).  Heads with
+// larger (outlier) channels take the three-digit path, exact to ~2^-22 of max|q|.
+constexpr float kTwoDigitMax = 0.375f;
 constexpr int NBAR = 2 * NS;       // stage barriers: stage it uses barrier it % NBAR, so each
                                    // barrier serves only one warp group (NBAR even)
 
@@ -360,7 +367,11 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
   if (tid == 0)
     for (int i = 0; i < NS && u0 + i < u1; ++i) issue(u0 + i);
 
-  uint32_t qa[NB][4];      // int8 digit fragments of this warp's 8 query heads
+  uint32_t qa[NB][4];      // int8 digits a (rows 0-7) and b (rows 8-15) of the 8 query heads
+  // int8 digit c (rows 0-7 of a second MMA whose rows 8-15 are zero), kept in local memory (L1)
+  // so that the two-digit path does not carry it in registers
+  volatile uint32_t qc[NB][2];
+  bool exact3 = false;     // this entry takes the three-digit / split-P path (warp-uniform)
   float fac = 0.f;         // per-head factor sigma/254 * scale * log2(e) (head g)
   float o[NB][2][4];       // O^T accumulators: [block][m-tile][frag]
   float m_run = -INFINITY, l_run = 0.f;
@@ -405,67 +416,15 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
   const int swk = g & 1;
   const int tok_k = (g >> 1) + 4 * (g & 1);  // token loaded for K column g
 
-  for (int u = u0 + grp; u < u1; u += GROUPS) {
+  // One unit (stage) of the CTA's range; EX: the three-digit query / split-P path.  The two
+  // paths are separate loops over an entry's units, chosen once per entry, so the two-digit
+  // loop carries none of the exact path's code or registers.
+  auto unit_step = [&](auto exact_tag, int u) -> bool {
+    constexpr bool EX = decltype(exact_tag)::value;
     const int it = u - u0;
     const int buf = it % NS;
     const int bar = it % NBAR;
     const uint32_t par = (uint32_t)(it / NBAR) & 1u;
-    int bu = b < 0 ? e_next : b;
-    while (u >= sm.prefix[bu + 1]) ++bu;
-    if (bu != b) {
-      owe_empty_until(bu);
-      e_next = bu + 1;
-      b = bu;
-      e_beg = a.kv_begin ? a.kv_begin[b] : 0;
-      e_end = a.kv_end[b] + a.end_add;
-      // ---- query digits: q ~= sigma * (d_a + d_b / 254), sigma = max|q| / 127 ------------
-      const float* qh = a.q + ((size_t)b * a.n_head + kh * G + g) * HD;
-      float amax = 0.f;
-      bool nonfinite = false;
-#pragma unroll
-      for (int c = 0; c < NB; ++c)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float x = qh[group_dim(c, 2 * q + (i >> 2), i & 3)];
-          amax = fmaxf(amax, fabsf(x));
-          nonfinite |= !isfinite(x);
-        }
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-      nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, 1) != 0;
-      nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, 2) != 0;
-      const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-#pragma unroll
-      for (int c = 0; c < NB; ++c) {
-        uint32_t da[2] = {0, 0}, db[2] = {0, 0};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float z = qh[group_dim(c, 2 * q + (i >> 2), i & 3)] * inv;
-          float ra = rintf(z);
-          ra = fminf(fmaxf(ra, -127.f), 127.f);
-          float rb = rintf((z - ra) * 254.0f);
-          rb = fminf(fmaxf(rb, -127.f), 127.f);
-          const int ia = (ra == ra) ? (int)ra : 0;
-          const int ib = (rb == rb) ? (int)rb : 0;
-          da[i >> 2] |= ((uint32_t)ia & 0xffu) << (8 * (i & 3));
-          db[i >> 2] |= ((uint32_t)ib & 0xffu) << (8 * (i & 3));
-        }
-        qa[c][0] = da[0];  // rows 0-7 (digit a), k 4q..4q+3   = group 2q
-        qa[c][1] = db[0];  // rows 8-15 (digit b), same k
-        qa[c][2] = da[1];  // rows 0-7, k 16+4q..               = group 2q+1
-        qa[c][3] = db[1];
-      }
-      fac = (amax / 127.0f) * (1.0f / 254.0f) * a.scale * kLog2e;
-      if (nonfinite) fac = __int_as_float(0x7fffffff);  // NaN: the head's output becomes NaN
-      m_run = -INFINITY;
-      l_run = 0.f;
-#pragma unroll
-      for (int c = 0; c < NB; ++c)
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) o[c][mt][e] = 0.f;
-    }
     const int t_start = e_beg + (u - sm.prefix[b]) * ST;
     const int ntok = min(ST, e_end - t_start);
 
@@ -475,7 +434,7 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
       if (lane == 0) atomicOr(a.status, kStatusTimeout);
       for (int k = 1; k < NS; ++k)
         if (u + k < u1) mbar_wait(&sm.full[(it + k) % NBAR], (uint32_t)((it + k) / NBAR) & 1u, kWaitNs);
-      return;
+      return false;
     }
     const uint8_t* kst = sm.stage[buf][0];
     const uint8_t* vst = sm.stage[buf][1];
@@ -504,6 +463,35 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
       // ---- S = Q K^T on int8 tensor cores: 2 n-tiles of 8 tokens ---------------------------
       float sacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
       const uint8_t* rec0 = kst + (16 * sub + tok_k) * TOKB + kh * REC;
+      if constexpr (EX) {
+#pragma unroll
+      for (int c = 0; c < NB; ++c) {
+        const float4 dk = wsk[4 * c];
+        const uint32_t qcf[4] = {qc[c][0], 0u, qc[c][1], 0u};
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const uint8_t* blk = rec0 + 8 * j * TOKB + c * kBlk;
+          uint32_t x, y;
+          if (c & 1) {
+            x = load_group<1>(blk, 2 * q + swk);
+            y = load_group<1>(blk, 2 * q + 1 - swk);
+          } else {
+            x = load_group<0>(blk, 2 * q + swk);
+            y = load_group<0>(blk, 2 * q + 1 - swk);
+          }
+          const uint32_t b0 = swk ? y : x, b1 = swk ? x : y;
+          int acc[4], acc3[4];
+          imma_16832(acc, qa[c], b0, b1);
+          imma_16832(acc3, qcf, b0, b1);
+          const float x0 = fmaf(__int2float_rn(acc3[0]), 1.0f / 254.0f,
+                                __int2float_rn(254 * acc[0] + acc[2]));
+          const float x1 = fmaf(__int2float_rn(acc3[1]), 1.0f / 254.0f,
+                                __int2float_rn(254 * acc[1] + acc[3]));
+          sacc[j][0] = fmaf(j ? dk.z : dk.x, x0, sacc[j][0]);
+          sacc[j][1] = fmaf(j ? dk.w : dk.y, x1, sacc[j][1]);
+        }
+      }
+      } else {
 #pragma unroll
       for (int c = 0; c < NB; ++c) {
         const float4 dk = wsk[4 * c];
@@ -526,6 +514,7 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
           sacc[j][0] = fmaf(j ? dk.z : dk.x, __int2float_rn(x0), sacc[j][0]);
           sacc[j][1] = fmaf(j ? dk.w : dk.y, __int2float_rn(x1), sacc[j][1]);
         }
+      }
       }
       // ---- online softmax (log2 domain) ----------------------------------------------------
       float p[2][2];
@@ -574,8 +563,10 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
 #pragma unroll
       for (int c = 0; c < NB; ++c) {
         const float4 dv = wsv[4 * c];
-        const uint32_t pb0 = pack_f16x2(p[0][0] * dv.x, p[0][1] * dv.y);
-        const uint32_t pb1 = pack_f16x2(p[1][0] * dv.z, p[1][1] * dv.w);
+        const float x00 = p[0][0] * dv.x, x01 = p[0][1] * dv.y;
+        const float x10 = p[1][0] * dv.z, x11 = p[1][1] * dv.w;
+        const uint32_t pb0 = pack_f16x2(x00, x01);
+        const uint32_t pb1 = pack_f16x2(x10, x11);
         uint32_t f0, f1, f8, f9;
         if (c & 1) {
           f0 = load_group<1>(vr0 + c * kBlk, g);
@@ -596,6 +587,16 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
                    codes_to_f16x2(hi01, 0x4140), codes_to_f16x2(hi01, 0x4342), pb0, pb1);
         hmma_16816(o[c][1], codes_to_f16x2(lo23, 0x4140), codes_to_f16x2(lo23, 0x4342),
                    codes_to_f16x2(hi23, 0x4140), codes_to_f16x2(hi23, 0x4342), pb0, pb1);
+        if constexpr (EX) {  // P' as f16 hi + lo
+          const __half2 hb0 = *reinterpret_cast<const __half2*>(&pb0);
+          const __half2 hb1 = *reinterpret_cast<const __half2*>(&pb1);
+          const uint32_t pl0 = pack_f16x2(x00 - __low2float(hb0), x01 - __high2float(hb0));
+          const uint32_t pl1 = pack_f16x2(x10 - __low2float(hb1), x11 - __high2float(hb1));
+          hmma_16816(o[c][0], codes_to_f16x2(lo01, 0x4140), codes_to_f16x2(lo01, 0x4342),
+                     codes_to_f16x2(hi01, 0x4140), codes_to_f16x2(hi01, 0x4342), pl0, pl1);
+          hmma_16816(o[c][1], codes_to_f16x2(lo23, 0x4140), codes_to_f16x2(lo23, 0x4342),
+                     codes_to_f16x2(hi23, 0x4140), codes_to_f16x2(hi23, 0x4342), pl0, pl1);
+        }
       }
     }
 
@@ -615,7 +616,85 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
     }
 
     // ---- this warp's last unit of the entry in this CTA: write its partial -----------------
-    if (u + GROUPS >= u1 || u + GROUPS >= sm.prefix[b + 1]) write_partial(b, false);
+    return true;
+  };
+  for (int u = u0 + grp; u < u1;) {
+    int bu = b < 0 ? e_next : b;
+    while (u >= sm.prefix[bu + 1]) ++bu;
+    if (bu != b) {
+      owe_empty_until(bu);
+      e_next = bu + 1;
+      b = bu;
+      e_beg = a.kv_begin ? a.kv_begin[b] : 0;
+      e_end = a.kv_end[b] + a.end_add;
+      // ---- query digits: q ~= sigma * (d_a + d_b / 254 [+ d_c / 254^2]), sigma = max|q| / 127.
+      //      The third digit (and the f16 hi/lo split of P in PV) is used by warps whose heads
+      //      have max|q| * scale above kTwoDigitMax: outlier channels, as post-norm / RoPE
+      //      queries can have, would otherwise cost the other channels their precision. ------
+      const float* qh = a.q + ((size_t)b * a.n_head + kh * G + g) * HD;
+      float amax = 0.f;
+      bool nonfinite = false;
+#pragma unroll
+      for (int c = 0; c < NB; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float x = qh[group_dim(c, 2 * q + (i >> 2), i & 3)];
+          amax = fmaxf(amax, fabsf(x));
+          nonfinite |= !isfinite(x);
+        }
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, 1) != 0;
+      nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, 2) != 0;
+      exact3 = __any_sync(0xffffffffu, amax * a.scale > kTwoDigitMax);
+      const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+#pragma unroll
+      for (int c = 0; c < NB; ++c) {
+        uint32_t da[2] = {0, 0}, db[2] = {0, 0}, dc[2] = {0, 0};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float z = qh[group_dim(c, 2 * q + (i >> 2), i & 3)] * inv;
+          const float ra = fminf(fmaxf(rintf(z), -127.f), 127.f);
+          const float r1 = (z - ra) * 254.0f;        // z - ra is exact
+          const float rb = fminf(fmaxf(rintf(r1), -127.f), 127.f);
+          const float rc =
+              exact3 ? fminf(fmaxf(rintf((r1 - rb) * 254.0f), -127.f), 127.f) : 0.f;
+          const int ia = (ra == ra) ? (int)ra : 0;
+          const int ib = (rb == rb) ? (int)rb : 0;
+          const int ic = (rc == rc) ? (int)rc : 0;
+          da[i >> 2] |= ((uint32_t)ia & 0xffu) << (8 * (i & 3));
+          db[i >> 2] |= ((uint32_t)ib & 0xffu) << (8 * (i & 3));
+          dc[i >> 2] |= ((uint32_t)ic & 0xffu) << (8 * (i & 3));
+        }
+        qa[c][0] = da[0];  // rows 0-7 (digit a), k 4q..4q+3   = group 2q
+        qa[c][1] = db[0];  // rows 8-15 (digit b), same k
+        qa[c][2] = da[1];  // rows 0-7, k 16+4q..               = group 2q+1
+        qa[c][3] = db[1];
+        if (exact3) {
+          qc[c][0] = dc[0];
+          qc[c][1] = dc[1];
+        }
+      }
+      fac = (amax / 127.0f) * (1.0f / 254.0f) * a.scale * kLog2e;
+      if (nonfinite) fac = __int_as_float(0x7fffffff);  // NaN: the head's output becomes NaN
+      m_run = -INFINITY;
+      l_run = 0.f;
+#pragma unroll
+      for (int c = 0; c < NB; ++c)
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[c][mt][e] = 0.f;
+    }
+    const int u_stop = min(u1, sm.prefix[b + 1]);
+    if (exact3) {
+      for (; u < u_stop; u += GROUPS)
+        if (!unit_step(std::true_type{}, u)) return;
+    } else {
+      for (; u < u_stop; u += GROUPS)
+        if (!unit_step(std::false_type{}, u)) return;
+    }
+    write_partial(b, false);
   }
   if constexpr (GROUPS > 1) owe_empty_until(find_batch(sm.prefix, B, u1 - 1) + 1);
 }
