@@ -306,41 +306,9 @@ __global__ void __launch_bounds__(256, 1) deltanet_step_persistent(DeltaNetArgs 
 // Prefill: the recurrence over n_tok tokens with the state held in registers.
 // Preparation pass: normalised q, k per (b, t, k head) and (beta, decay) per (b, t, v head).
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) deltanet_prep_kernel(DeltaNetArgs a, float* qn, float* kn,
-                                                            float2* gates, float* lgs,
-                                                            float q_scale) {
-  // blockIdx.x = (b * n_tok + t) ; threads cover the k heads (warp per head) then the gates
-  const int bt = blockIdx.x;
-  const int b = bt / a.n_tok, t = bt - b * a.n_tok;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int hk = warp; hk < a.n_kh; hk += blockDim.x >> 5) {
-    const float* qg = a.q + (size_t)b * a.q_bs + (size_t)t * a.q_ts + (size_t)hk * a.dk;
-    const float* kg = a.k + (size_t)b * a.k_bs + (size_t)t * a.k_ts + (size_t)hk * a.dk;
-    float sq = 0.f, sk = 0.f;
-    for (int i = lane; i < a.dk; i += 32) {
-      sq = fmaf(qg[i], qg[i], sq);
-      sk = fmaf(kg[i], kg[i], sk);
-    }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    const float qs = q_scale / sqrtf(sq + a.eps), ks = 1.0f / sqrtf(sk + a.eps);
-    float* qo = qn + ((size_t)bt * a.n_kh + hk) * a.dk;
-    float* ko = kn + ((size_t)bt * a.n_kh + hk) * a.dk;
-    for (int i = lane; i < a.dk; i += 32) {
-      qo[i] = qg[i] * qs;
-      ko[i] = kg[i] * ks;
-    }
-  }
-  for (int h = threadIdx.x; h < a.n_vh; h += blockDim.x) {
-    const size_t gi = (size_t)b * a.g_bs + (size_t)t * a.g_ts + h;
-    const float lg = log_decay_of(a.alpha_raw[gi], a.dt_bias[h], a.ssm_a[h]);
-    gates[(size_t)bt * a.n_vh + h] = make_float2(sigmoidf_(a.beta_raw[gi]), expf(lg));
-    if (lgs) lgs[(size_t)bt * a.n_vh + h] = lg;
-  }
-}
-
-// The same preparation with one warp per (b, t, k head) and 16-byte accesses, for dense q / k
-// rows with 16-byte aligned starts (dk <= 256); the gates take one thread per (b, t, v head).
+// One warp per (b, t, k head) with 16-byte accesses (q / k rows are dense and 16-byte aligned:
+// the entry points reject misaligned device arrays and dk is 64, 128 or 256); the gates take
+// one thread per (b, t, v head).
 __global__ void __launch_bounds__(256) deltanet_prep_vec_kernel(DeltaNetArgs a, float* qn,
                                                                 float* kn, float2* gates,
                                                                 float* lgs, float q_scale) {
@@ -457,27 +425,6 @@ __global__ void __launch_bounds__(256) deltanet_prefill_kernel(DeltaNetArgs a, c
   if (bad) atomicOr(a.status, kStatusNonFinite);
 }
 
-// y = RMSNorm(o) * ssm_norm * SiLU(z) per (b, t, v head); one warp per row of dv.
-__global__ void __launch_bounds__(256) deltanet_epilogue_kernel(DeltaNetArgs a) {
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  const int rows = a.n_batch * a.n_tok * a.n_vh;
-  if (row >= rows) return;
-  const int h = row % a.n_vh, bt = row / a.n_vh;
-  const int b = bt / a.n_tok, t = bt - b * a.n_tok;
-  const size_t off = (size_t)b * a.o_bs + (size_t)t * a.o_ts + (size_t)h * a.dv;
-  float sq = 0.f;
-  for (int j = lane; j < a.dv; j += 32) sq = fmaf(a.o[off + j], a.o[off + j], sq);
-  sq = warp_sum(sq);
-  const float scale = 1.0f / sqrtf(sq / (float)a.dv + a.eps);
-  bool bad = false;
-  for (int j = lane; j < a.dv; j += 32) {
-    const float yv = a.o[off + j] * scale * a.ssm_norm[j] * siluf_(a.z[off + j]);
-    a.y[off + j] = yv;
-    bad |= !isfinite(yv);
-  }
-  if (bad) atomicOr(a.status, kStatusNonFinite);
-}
-
 // ---------------------------------------------------------------------------------------------
 // conv1d + SiLU prologue (llm_ops.rs:122-137): per (sequence, channel), a sequential fma chain
 // over the k_sz - 1 history rows and the new input, then the history shifts by one row.
@@ -561,18 +508,10 @@ cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, int al
   // the chunked kernel takes q unit-normalised (its f16 products want |q| <= 1) and applies
   // q_scale to the products; the sequential kernel takes it folded in
   const float qscale = chunked ? 1.0f : a.q_scale;
-  const bool vec = a.dk % 4 == 0 && a.dk <= 256 && a.q_ts % 4 == 0 && a.q_bs % 4 == 0 &&
-                   a.k_ts % 4 == 0 && a.k_bs % 4 == 0 &&
-                   ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k)) & 15u) == 0;
-  if (vec) {
-    const long long warps = (long long)bt * a.n_kh, gthreads = (long long)bt * a.n_vh;
-    const long long blocks = std::max((warps + 7) / 8, (gthreads + 255) / 256);
-    deltanet_prep_vec_kernel<<<(unsigned)blocks, 256, 0, st>>>(a, qn, kn, gates,
-                                                              chunked ? lgs : nullptr, qscale);
-  } else {
-    deltanet_prep_kernel<<<(unsigned)bt, 128, 0, st>>>(a, qn, kn, gates, chunked ? lgs : nullptr,
-                                                       qscale);
-  }
+  const long long warps = (long long)bt * a.n_kh, gthreads = (long long)bt * a.n_vh;
+  const long long blocks = std::max((warps + 7) / 8, (gthreads + 255) / 256);
+  deltanet_prep_vec_kernel<<<(unsigned)blocks, 256, 0, st>>>(a, qn, kn, gates,
+                                                            chunked ? lgs : nullptr, qscale);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (chunked) {
@@ -587,10 +526,7 @@ cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, int al
     }
     e = cudaGetLastError();
   }
-  if (e != cudaSuccess || !a.y) return e;
-  const int rows = a.n_batch * a.n_tok * a.n_vh;
-  deltanet_epilogue_kernel<<<(rows + 7) / 8, 256, 0, st>>>(a);
-  return cudaGetLastError();
+  return e;
 }
 
 cudaError_t launch_deltanet_conv(const float* x, const float* w, float* conv_state, float* out,

@@ -122,7 +122,7 @@ struct DeltaNetArgs {
 // One token per sequence (t = 0), state streamed from / to HBM.
 cudaError_t launch_deltanet_step(const DeltaNetArgs& a, cudaStream_t stream);
 // n_tok tokens per sequence with the state held on chip; needs deltanet_prefill_scratch_bytes of
-// device scratch.  Writes o (and y with the epilogue when y != nullptr).
+// device scratch.  Writes o (y is not used: the prefill returns o before the epilogue).
 // allow_chunk: dk 128 and dv a multiple of 64 with at least 64 tokens run the chunked (WY)
 // tensor-core kernel (deltanet_chunk.cu); otherwise the sequential on-chip recurrence.
 size_t deltanet_prefill_scratch_bytes(const DeltaNetArgs& a);
