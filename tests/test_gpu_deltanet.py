@@ -128,8 +128,9 @@ def test_deltanet_prefill_matches_token_by_token_oracle(ctx, B, T, n_kh, n_vh, d
 
 
 @pytest.mark.parametrize("B,T,n_kh,n_vh,dv,generic", [
-    (2, 300, 2, 4, 64, False),      # chunked (WY) tensor-core path: 5 chunks, the last partial
-    (1, 4096, 2, 2, 128, False),    # config-5b prompt length, 64 chunks
+    (2, 300, 2, 4, 64, False),      # chunked (WY) mma.sync kernel: 5 chunks, the last partial
+    (2, 300, 2, 4, 128, False),     # chunked tcgen05 kernel (dv 128): GQA, the last chunk partial
+    (1, 4096, 2, 2, 128, False),    # config-5b prompt length, 64 chunks (tcgen05 kernel)
     (2, 300, 2, 4, 64, True),       # the sequential kernel on the same shapes
 ])
 def test_deltanet_prefill_chunked_matches_sequential_oracle(ctx, B, T, n_kh, n_vh, dv, generic):

@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(HERE, "libvxg_attn_cuda.so")
 SOURCES = ["abi.cu", "q8_append.cu", "decode_attn.cu", "deltanet.cu", "prep.cu", "noalloc.cu",
-           "prefill_attn.cu", "prefill_tc.cu", "deltanet_chunk.cu", "peer.cu"]
+           "prefill_attn.cu", "prefill_tc.cu", "deltanet_chunk.cu", "deltanet_tc.cu", "peer.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

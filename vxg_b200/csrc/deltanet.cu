@@ -15,6 +15,7 @@
 // floats each at dk = 128, interleaved so 8 lanes cover 128 contiguous bytes per float4 load),
 // 32 rows per pass, all passes loaded before any arithmetic so the CTA keeps its whole state in
 // flight; row dot products are 3-step shuffle reductions inside the 8-lane group.
+#include "dn_gates.cuh"
 #include "kernels.h"
 
 #include <algorithm>
@@ -22,14 +23,7 @@
 namespace vxg {
 
 namespace {
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x / (1.0f + expf(-x)); }
-// llm_ops.rs:156-165
-__device__ __forceinline__ float log_decay_of(float alpha_raw, float dt_bias, float A) {
-  const float x = alpha_raw + dt_bias;
-  const float sp = x > 20.0f ? x : (x < -20.0f ? expf(x) : logf(1.0f + expf(x)));
-  return sp * A;
-}
 __device__ __forceinline__ float decay_of(float alpha_raw, float dt_bias, float A) {
   return expf(log_decay_of(alpha_raw, dt_bias, A));
 }
@@ -499,6 +493,9 @@ size_t deltanet_prefill_scratch_bytes(const DeltaNetArgs& a) {
 cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, int allow_chunk,
                                     cudaStream_t st) {
   if (a.n_batch == 0 || a.n_tok == 0 || a.n_vh == 0) return cudaSuccess;
+  // dk = dv = 128 (the Qwen3.5 shape): the tcgen05 / TMEM chunk kernel, which forms the norms
+  // and gates itself (no preparation pass)
+  if (allow_chunk && deltanet_chunk_tc_supported(a)) return launch_deltanet_chunk_tc(a, st);
   const size_t bt = (size_t)a.n_batch * a.n_tok;
   float* qn = static_cast<float*>(scratch);
   float* kn = qn + bt * a.n_kh * a.dk;

@@ -124,7 +124,8 @@ cudaError_t launch_deltanet_step(const DeltaNetArgs& a, cudaStream_t stream);
 // n_tok tokens per sequence with the state held on chip; needs deltanet_prefill_scratch_bytes of
 // device scratch.  Writes o (y is not used: the prefill returns o before the epilogue).
 // allow_chunk: dk 128 and dv a multiple of 64 with at least 64 tokens run the chunked (WY)
-// tensor-core kernel (deltanet_chunk.cu); otherwise the sequential on-chip recurrence.
+// form (deltanet_tc.cu for dv = 128, deltanet_chunk.cu otherwise); other shapes, or
+// allow_chunk = 0, the sequential on-chip recurrence.
 size_t deltanet_prefill_scratch_bytes(const DeltaNetArgs& a);
 cudaError_t launch_deltanet_prefill(const DeltaNetArgs& a, void* scratch, int allow_chunk,
                                     cudaStream_t stream);
@@ -134,6 +135,12 @@ bool deltanet_chunk_supported(const DeltaNetArgs& a);
 size_t deltanet_chunk_smem_bytes();
 cudaError_t launch_deltanet_chunk(const DeltaNetArgs& a, const float* qn, const float* kn,
                                   const float2* gates, const float* lgs, cudaStream_t stream);
+// deltanet_tc.cu: the same chunked form on tcgen05 / TMEM for dk = dv = 128 (one CTA per
+// (sequence, v head) with the whole state in tensor memory); reads the raw arguments (norms
+// and gates on chip), so it needs no preparation pass and no scratch.
+bool deltanet_chunk_tc_supported(const DeltaNetArgs& a);
+size_t deltanet_chunk_tc_smem_bytes();
+cudaError_t launch_deltanet_chunk_tc(const DeltaNetArgs& a, cudaStream_t stream);
 // conv1d + SiLU over the rolling history (llm_ops.rs:122-137), batched.
 cudaError_t launch_deltanet_conv(const float* x, const float* w, float* conv_state, float* out,
                                  int n_batch, int conv_ch, int k_sz, cudaStream_t stream);
