@@ -718,7 +718,7 @@ def run_dnet_prefill(args, world, rank, local):
     """BASELINE config 5b: gated-DeltaNet prefill of 8 prompts x 8192 tokens per GPU, 32 heads,
     dk = dv = 128, the decode config's distributions (q, k, v N(0,1), beta = sigmoid(N(0,1)),
     decay exp(-softplus(N(0,1)))).  One step = vxg_attn_cuda_deltanet_prefill over all prompts
-    (chunked WY form, 64-token chunks, state rows held on chip)."""
+    (chunked WY form, 64-token chunks, one tcgen05 kernel with the state in tensor memory)."""
     import torch
     import torch.distributed as dist
     import vxg_b200
@@ -765,13 +765,15 @@ def run_dnet_prefill(args, world, rank, local):
         "config": {"workload": f"config5b: DeltaNet prefill, {B} prompts x 8192 tokens per GPU, "
                                "32 heads, dk=dv=128, state N(0,0.02^2) on chip",
                    "l2": "inputs larger than L2 (4.3 GB of q/k/v/o per step)"},
-        "roofline": {"kernel": "deltanet_chunk_kernel", "bound": "tensor", "achieved": ach,
+        "roofline": {"kernel": "deltanet_chunk_tc_kernel", "bound": "tensor", "achieved": ach,
                      "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                      "peak_kind": peak_kind + " (sustained bf16)",
                      "flop_per_launch": 2 * mac,
-                     "note": "FLOPs of the chunked (WY, C=64) algorithm, which the kernel "
-                             "runs on mma.sync m16n8k16 (f16, bf16 and hi/lo-split bf16)"},
-        "gpu_launches": 3 * K, "clocks": sampler.summary(),
+                     "note": "FLOPs of the chunked (WY, C=64) algorithm, counted once; the "
+                             "kernel runs its products on tcgen05 (f16, bf16 and hi/lo-split "
+                             "bf16, so up to 3x these FLOPs on the tensor pipe) and forms the "
+                             "norms, gates and the triangular inverse on chip"},
+        "gpu_launches": K, "clocks": sampler.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_dnet_prefill(q, k, v, br, ar, A, dt, state0)

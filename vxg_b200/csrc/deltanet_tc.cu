@@ -18,8 +18,9 @@
 //   W^T = R^T T^T           hi/lo-split bf16                           (the triangular solve)
 //   S += W^T (e^{L_C - L} K)  hi/lo-split bf16, after S *= gamma_C      (the state update)
 // These are the operand formats of the mma.sync chunk kernel (deltanet_chunk.cu), chosen by a
-// model of every product's rounding against the f64 recurrence; T itself is formed in f32 on
-// the CUDA cores (16 x 16 diagonal blocks by substitution, then two merges of block products).
+// model of every product's rounding against the f64 recurrence; T itself is formed from f32 16 x 16
+// diagonal blocks (substitution on the CUDA cores) and two merges of block products on mma.sync
+// with the same hi/lo-split bf16 operands.
 // S0, R^T and W^T enter their MMAs as A operands from tensor memory (bf16 pairs); K, Q, T and P
 // are 128-byte-swizzled shared-memory tiles.  Tensor memory (512 columns):
 //   S [0,128) f32 | S0 hi [128,192) lo [192,256) | Z [256,320) then W^T hi/lo pairs |
@@ -114,6 +115,42 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
                "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
                "r"(r[7])
                : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// One warp: acc (16 x 16, two 8-column tiles) += A (16 x K, row-major, leading dimension lda) *
+// B (K x 16, leading dimension ldb), both f32 in shared memory, as hi/lo-split bf16 products
+// (hi.hi + hi.lo + lo.hi).  acc[nt][e]: row g + 8 (e >> 1), column 8 nt + 2 q + (e & 1).
+template <int K>
+__device__ __forceinline__ void mma16x16_x3(float (&acc)[2][4], const float* A, int lda,
+                                            const float* B, int ldb, int lane) {
+  const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    uint32_t ah[4], al[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {  // a0: row g, k 2q | a1: row g+8 | a2: row g, k 2q+8 | a3
+      const float* ap = A + (g + 8 * (r & 1)) * lda + k0 + 2 * q + 8 * (r >> 1);
+      split_bf16(ap[0], ap[1], ah[r], al[r]);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const float* bp = B + (k0 + 2 * q) * ldb + 8 * nt + g;
+      uint32_t bh0, bl0, bh1, bl1;
+      split_bf16(bp[0], bp[ldb], bh0, bl0);
+      split_bf16(bp[8 * ldb], bp[9 * ldb], bh1, bl1);
+      mma_bf16_16816(acc[nt], al, bh0, bh1);
+      mma_bf16_16816(acc[nt], ah, bl0, bl1);
+      mma_bf16_16816(acc[nt], ah, bh0, bh1);
+    }
+  }
 }
 
 }  // namespace dntc
@@ -223,17 +260,30 @@ __global__ void __launch_bounds__(dntc::THREADS, 1) deltanet_chunk_tc_kernel(Del
   // gates of chunk cc (warp 1): beta, and the inclusive scan of the log2 decays, into buffer
   // cc & 1; padding tokens get beta 0 and decay 1
   const float gA = a.ssm_a[h], gdt = a.dt_bias[h];
-  auto form_gates = [&](int cc) {
-    const int t = cc * C + 2 * lane, gb = cc & 1;
+  // (warp 1 loads the raw inputs of chunk cc + 1 into registers once chunk cc's are formed)
+  float gar0 = 0.f, gar1 = 0.f, gbr0 = 0.f, gbr1 = 0.f;
+  auto load_raw_gates = [&](int cc) {
+    const int t = cc * C + 2 * lane;
     const size_t gi = (size_t)b * a.g_bs + (size_t)t * a.g_ts + h;
-    float l0 = 0.f, l1 = 0.f, be0 = 0.f, be1 = 0.f;
     if (t < a.n_tok) {
-      l0 = log_decay_of(a.alpha_raw[gi], gdt, gA) * kLog2e;
-      be0 = sigmoidf_(a.beta_raw[gi]);
+      gar0 = a.alpha_raw[gi];
+      gbr0 = a.beta_raw[gi];
     }
     if (t + 1 < a.n_tok) {
-      l1 = log_decay_of(a.alpha_raw[gi + a.g_ts], gdt, gA) * kLog2e;
-      be1 = sigmoidf_(a.beta_raw[gi + a.g_ts]);
+      gar1 = a.alpha_raw[gi + a.g_ts];
+      gbr1 = a.beta_raw[gi + a.g_ts];
+    }
+  };
+  auto form_gates = [&](int cc) {
+    const int t = cc * C + 2 * lane, gb = cc & 1;
+    float l0 = 0.f, l1 = 0.f, be0 = 0.f, be1 = 0.f;
+    if (t < a.n_tok) {
+      l0 = log_decay_of(gar0, gdt, gA) * kLog2e;
+      be0 = sigmoidf_(gbr0);
+    }
+    if (t + 1 < a.n_tok) {
+      l1 = log_decay_of(gar1, gdt, gA) * kLog2e;
+      be1 = sigmoidf_(gbr1);
     }
     float s = l0 + l1;
 #pragma unroll
@@ -251,7 +301,11 @@ __global__ void __launch_bounds__(dntc::THREADS, 1) deltanet_chunk_tc_kernel(Del
     sm.rdec[gb][2 * lane] = exp2f(LC - (s - l1));
     sm.rdec[gb][2 * lane + 1] = exp2f(LC - s);
   };
-  if (warp == 1) form_gates(0);
+  if (warp == 1) {
+    load_raw_gates(0);
+    form_gates(0);
+    if (n_chunks > 1) load_raw_gates(1);
+  }
   // raw V rows of a chunk ([64][128] f32) in the space of A / T, which are dead from the W^T
   // MMA of one chunk to the readout of the next
   float* stage_v = &sm.af[0][0];
@@ -345,7 +399,10 @@ __global__ void __launch_bounds__(dntc::THREADS, 1) deltanet_chunk_tc_kernel(Del
       }
       tc::mma_commit(&sm.mma_bar);
     }
-    if (warp == 1 && c + 1 < n_chunks) form_gates(c + 1);  // while the MMAs run
+    if (warp == 1 && c + 1 < n_chunks) {  // while the MMAs run
+      form_gates(c + 1);
+      if (c + 2 < n_chunks) load_raw_gates(c + 2);
+    }
     if (!wait_mma()) break;
     if (c + 1 < n_chunks) issue_stage(c + 1);  // the K / Q tiles are consumed
     // ---- Z -> A (lanes 0-63) and P (lanes 64-127); X -> R --------------------------------------
@@ -403,9 +460,15 @@ __global__ void __launch_bounds__(dntc::THREADS, 1) deltanet_chunk_tc_kernel(Del
       tmem_st8(tl + TM_X + 32 + tc0 / 2, rl);
     }
     __syncthreads();
-    // ---- T = (I + A)^-1: diagonal 16 x 16 blocks, thread = (block, column) -------------------
-    // (the upper-right 16 x 16 blocks of T's two 32 x 32 diagonal blocks, read by the 32-row
-    // merge, are zeroed here: the staged V rows of the previous chunk overwrote them)
+    // ---- T = (I + A)^-1 -------------------------------------------------------------------
+    // Diagonal 16 x 16 blocks by forward substitution, thread = (block, column): warp 0 inverts
+    // blocks 0 and 1, warp 1 blocks 2 and 3.  Below the diagonal, by merges of lower-triangular
+    // blocks: T [[X, 0], [Y, Z]] has the off-diagonal block -Z Y' X with Y' the off-diagonal block
+    // of I + A.  Warp w then merges its pair, T_{2w+1,2w} = -T_{2w+1,2w+1} A_{2w+1,2w} T_{2w,2w},
+    // and four warps the 32-row merge T[32:64, 0:32] = -T[32:64, 32:64] A[32:64, 0:32] T[0:32, 0:32],
+    // on mma.sync with hi/lo-split bf16 operands.  The upper-right 16 x 16 blocks of the two
+    // 32 x 32 diagonal blocks, read by that merge, are zeroed here (the staged V rows of the
+    // previous chunk overwrote them).
     if (tid >= 64 && tid < 64 + 2 * 256 / 4) {
       const int i = tid - 64, bi = i >> 6, r = (i >> 2) & 15, c4 = 4 * (i & 3);
       float* z = &sm.tf[32 * bi + r][32 * bi + 16 + c4];
@@ -422,66 +485,45 @@ __global__ void __launch_bounds__(dntc::THREADS, 1) deltanet_chunk_tc_kernel(Del
         for (int i = r + 1; i < 16; ++i) col[i] = fmaf(-sm.af[o + i][o + r], col[r], col[i]);
 #pragma unroll
       for (int r = 0; r < 16; ++r) sm.tf[o + r][o + cl] = col[r];
+      __syncwarp();
+      const int ob = 32 * warp;  // this warp's pair: T_00 at (ob, ob), A_10 at (ob + 16, ob)
+      const int g = lane >> 2, q = lane & 3;
+      float m[2][4] = {};
+      mma16x16_x3<16>(m, &sm.af[ob + 16][ob], C + 1, &sm.tf[ob][ob], C + 1, lane);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sm.mt[warp][g + 8 * (e >> 1)][8 * nt + 2 * q + (e & 1)] = m[nt][e];
+      __syncwarp();
+      float t2[2][4] = {};
+      mma16x16_x3<16>(t2, &sm.tf[ob + 16][ob + 16], C + 1, &sm.mt[warp][0][0], 17, lane);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          sm.tf[ob + 16 + g + 8 * (e >> 1)][ob + 8 * nt + 2 * q + (e & 1)] = -t2[nt][e];
     }
     __syncthreads();
-    // Below the diagonal, by two merges of lower-triangular blocks: T [[X, 0], [Y, Z]] has the
-    // off-diagonal block -Z Y' X with Y' the off-diagonal block of I + A.  First the 16-row merges
-    // T_10 = -T_11 A_10 T_00 and T_32 = -T_33 A_32 T_22, then the 32-row merge
-    // T[32:64, 0:32] = -T[32:64, 32:64] A[32:64, 0:32] T[0:32, 0:32]; the diagonal blocks hold zeros
-    // above their diagonals, so the inner loops run over whole blocks.
-    for (int e = tid; e < 2 * 256; e += THREADS) {   // M = A_{i,i-1} T_{i-1,i-1}, i = 1, 3
-      const int bi = e >> 8, r = (e >> 4) & 15, cl = e & 15;
-      const int o = 32 * bi;                          // T_00 at o, A_10 at (o + 16, o)
-      float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+    if (warp < 4) {  // M = A[32:64, 0:32] T[0:32, 0:32], warp = 16 x 16 tile (rt, ct)
+      const int rt = warp >> 1, ct = warp & 1, g = lane >> 2, q = lane & 3;
+      float m[2][4] = {};
+      mma16x16_x3<32>(m, &sm.af[32 + 16 * rt][0], C + 1, &sm.tf[0][16 * ct], C + 1, lane);
 #pragma unroll
-      for (int q = 0; q < 16; q += 4) {
-        m0 = fmaf(sm.af[o + 16 + r][o + q], sm.tf[o + q][o + cl], m0);
-        m1 = fmaf(sm.af[o + 16 + r][o + q + 1], sm.tf[o + q + 1][o + cl], m1);
-        m2 = fmaf(sm.af[o + 16 + r][o + q + 2], sm.tf[o + q + 2][o + cl], m2);
-        m3 = fmaf(sm.af[o + 16 + r][o + q + 3], sm.tf[o + q + 3][o + cl], m3);
-      }
-      sm.mt[bi][r][cl] = (m0 + m1) + (m2 + m3);
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          sm.mt32[16 * rt + g + 8 * (e >> 1)][16 * ct + 8 * nt + 2 * q + (e & 1)] = m[nt][e];
     }
     __syncthreads();
-    for (int e = tid; e < 2 * 256; e += THREADS) {   // T_{i,i-1} = -T_ii M
-      const int bi = e >> 8, r = (e >> 4) & 15, cl = e & 15;
-      const int o = 32 * bi;
-      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    if (warp < 4) {  // T[32:64, 0:32] = -T[32:64, 32:64] M
+      const int rt = warp >> 1, ct = warp & 1, g = lane >> 2, q = lane & 3;
+      float t2[2][4] = {};
+      mma16x16_x3<32>(t2, &sm.tf[32 + 16 * rt][32], C + 1, &sm.mt32[0][16 * ct], 33, lane);
 #pragma unroll
-      for (int q = 0; q < 16; q += 4) {
-        s0 = fmaf(sm.tf[o + 16 + r][o + 16 + q], sm.mt[bi][q][cl], s0);
-        s1 = fmaf(sm.tf[o + 16 + r][o + 16 + q + 1], sm.mt[bi][q + 1][cl], s1);
-        s2 = fmaf(sm.tf[o + 16 + r][o + 16 + q + 2], sm.mt[bi][q + 2][cl], s2);
-        s3 = fmaf(sm.tf[o + 16 + r][o + 16 + q + 3], sm.mt[bi][q + 3][cl], s3);
-      }
-      sm.tf[o + 16 + r][o + cl] = -((s0 + s1) + (s2 + s3));
-    }
-    __syncthreads();
-    // 32-row merge: M (32 x 32) = A[32:64, 0:32] T[0:32, 0:32], then T[32:64, 0:32] = -T_lr M
-    for (int e = tid; e < 32 * 32; e += THREADS) {
-      const int r = e >> 5, cl = e & 31;
-      float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int q = 0; q < 32; q += 4) {
-        m0 = fmaf(sm.af[32 + r][q], sm.tf[q][cl], m0);
-        m1 = fmaf(sm.af[32 + r][q + 1], sm.tf[q + 1][cl], m1);
-        m2 = fmaf(sm.af[32 + r][q + 2], sm.tf[q + 2][cl], m2);
-        m3 = fmaf(sm.af[32 + r][q + 3], sm.tf[q + 3][cl], m3);
-      }
-      sm.mt32[r][cl] = (m0 + m1) + (m2 + m3);
-    }
-    __syncthreads();
-    for (int e = tid; e < 32 * 32; e += THREADS) {
-      const int r = e >> 5, cl = e & 31;
-      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-      for (int q = 0; q < 32; q += 4) {
-        s0 = fmaf(sm.tf[32 + r][32 + q], sm.mt32[q][cl], s0);
-        s1 = fmaf(sm.tf[32 + r][32 + q + 1], sm.mt32[q + 1][cl], s1);
-        s2 = fmaf(sm.tf[32 + r][32 + q + 2], sm.mt32[q + 2][cl], s2);
-        s3 = fmaf(sm.tf[32 + r][32 + q + 3], sm.mt32[q + 3][cl], s3);
-      }
-      sm.tf[32 + r][cl] = -((s0 + s1) + (s2 + s3));
+        for (int e = 0; e < 4; ++e)
+          sm.tf[32 + 16 * rt + g + 8 * (e >> 1)][16 * ct + 8 * nt + 2 * q + (e & 1)] = -t2[nt][e];
     }
     __syncthreads();
     // T -> bf16 hi / lo tiles, row t, 8 values of i per item (zero above the diagonal)
