@@ -22,7 +22,6 @@
 #include "kernels.h"
 
 #include <algorithm>
-#include <type_traits>
 #include <utility>
 
 namespace vxg {
@@ -290,70 +289,24 @@ __device__ __forceinline__ UnitInfo unit_info(const DecodeArgs& a, const int* pr
   return r;
 }
 
-// Warp roles: warp = kv head (bit 0) | 16-token sub-tile (bits 1-2).  Warps only meet at the
-// stage ring: each waits for a stage's bulk copy, and the last warp done with a buffer refills
-// it, so warps drift freely within the ring (no block-wide barrier in the steady state).  At
-// the end of a (batch entry, CTA) segment every warp writes its own (m, l, O) partial; the
-// combine kernel merges them.  Partial slot of warp (kh, sub) in CTA i for entry b:
-// (i + b) * SUBS + sub, heads kh*8 .. kh*8+7, O stored [dim][head].
-__global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(DecodeArgs a,
-                                                                       Partials part) {
+// The calling warp's share of units [u, u_stop) of batch entry b (one kv head, one 16-token
+// sub-tile of every stage), ending with its (m, l, O) partial.  EX: the three-digit query split
+// and the f16 hi/lo split of P (heads with outlier channels); otherwise two digits and one f16
+// P.  The two instances are separate functions (the exact one is not inlined), so the two-digit
+// loop is compiled as if the exact path did not exist.  Returns false if a stage wait gave up.
+template <bool EX>
+__device__ __forceinline__ bool fast_entry(const DecodeArgs& a, const Partials& part, int b, int u,
+                                           int u_stop, int u0, int u1, float amax,
+                                           bool nonfinite) {
   using namespace fast;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
-  const int kh = warp & 1, sub = (warp >> 1) % SPK, grp = warp / WPS;
-  const int slot_sub = warp >> 1;  // grp * SPK + sub
-  const int B = a.n_batch;
-  grid_dep_trigger();  // the combine pass may be scheduled as this grid's CTAs retire
-  // Launched to overlap the previous kernel's tail: everything it reads or writes in global
-  // memory (positions, cache, partial slots and the published ranges a previous combine may
-  // still be reading) waits until that kernel has completed.
-  grid_dep_wait();
-
-  // ---- unit prefix over the batch (warp 0: serial per lane chunk + warp scan) -----------
-  if (warp == 0) {
-    const int per = (B + 31) / 32;
-    int run = 0;
-    for (int i = 0; i < per; ++i) {
-      const int bb = lane * per + i;
-      if (bb < B) run += (entry_len(a, bb) + ST - 1) / ST;
-    }
-    int incl = run;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    int acc = incl - run;
-    for (int i = 0; i < per; ++i) {
-      const int bb = lane * per + i;
-      if (bb < B) {
-        sm.prefix[bb] = acc;
-        acc += (entry_len(a, bb) + ST - 1) / ST;
-      }
-    }
-    if (lane == 31) sm.prefix[B] = incl;
-    __syncwarp();
-    if (blockIdx.x == 0) {  // published for the combine pass: unit prefix and CTA unit ranges
-      for (int i = lane; i <= B; i += 32) part.prefix[i] = sm.prefix[i];
-      const long long Utot = sm.prefix[B];
-      for (int i = lane; i <= (int)gridDim.x; i += 32)
-        part.prefix[B + 1 + i] = (int)((long long)i * Utot / gridDim.x);
-    }
-  }
-  if (tid == 0) {
-    for (int i = 0; i < NBAR; ++i) mbar_init(&sm.full[i], 1);
-    for (int i = 0; i < NS; ++i) sm.done[i] = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-  const long long U = sm.prefix[B];
-  const int u0 = (int)((long long)blockIdx.x * U / gridDim.x);
-  const int u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
-  if (u0 >= u1) return;
-
+  const int kh = warp & 1, sub = (warp >> 1) % SPK;
+  const int slot_sub = warp >> 1;
+  const int e_beg = a.kv_begin ? a.kv_begin[b] : 0;
+  const int e_end = a.kv_end[b] + a.end_add;
   auto issue = [&](int u) {  // unit u -> buffer (u - u0) % NS, barrier (u - u0) % NBAR
     const UnitInfo ui = unit_info(a, sm.prefix, u);
     const uint32_t bytes = (uint32_t)ui.ntok * TOKB;
@@ -363,24 +316,48 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
     mbar_arrive_expect_tx(bar, 2 * bytes);
     bulk_g2s(sm.stage[buf][0], a.k_pool + off, bytes, bar);
     bulk_g2s(sm.stage[buf][1], a.v_pool + off, bytes, bar);
-  };
-  if (tid == 0)
-    for (int i = 0; i < NS && u0 + i < u1; ++i) issue(u0 + i);
-
-  uint32_t qa[NB][4];      // int8 digits a (rows 0-7) and b (rows 8-15) of the 8 query heads
-  // int8 digit c (rows 0-7 of a second MMA whose rows 8-15 are zero), kept in local memory (L1)
-  // so that the two-digit path does not carry it in registers
-  volatile uint32_t qc[NB][2];
-  bool exact3 = false;     // this entry takes the three-digit / split-P path (warp-uniform)
-  float fac = 0.f;         // per-head factor sigma/254 * scale * log2(e) (head g)
+  };  uint32_t qa[NB][4];      // int8 digits a (rows 0-7) and b (rows 8-15) of the 8 query heads
+  uint32_t qc[NB][2];      // EX: digit c (rows 0-7 of a second MMA whose rows 8-15 are zero)
+  // ---- query digits: q ~= sigma * (d_a + d_b / 254 [+ d_c / 254^2]), sigma = max|q| / 127 ----
+      const float* qh = a.q + ((size_t)b * a.n_head + kh * G + g) * HD;
+      const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+#pragma unroll
+      for (int c = 0; c < NB; ++c) {
+        uint32_t da[2] = {0, 0}, db[2] = {0, 0}, dc[2] = {0, 0};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float z = qh[group_dim(c, 2 * q + (i >> 2), i & 3)] * inv;
+          const float ra = fminf(fmaxf(rintf(z), -127.f), 127.f);
+          const float r1 = (z - ra) * 254.0f;        // z - ra is exact
+          const float rb = fminf(fmaxf(rintf(r1), -127.f), 127.f);
+          const float rc =
+              EX ? fminf(fmaxf(rintf((r1 - rb) * 254.0f), -127.f), 127.f) : 0.f;
+          const int ia = (ra == ra) ? (int)ra : 0;
+          const int ib = (rb == rb) ? (int)rb : 0;
+          const int ic = (rc == rc) ? (int)rc : 0;
+          da[i >> 2] |= ((uint32_t)ia & 0xffu) << (8 * (i & 3));
+          db[i >> 2] |= ((uint32_t)ib & 0xffu) << (8 * (i & 3));
+          dc[i >> 2] |= ((uint32_t)ic & 0xffu) << (8 * (i & 3));
+        }
+        qa[c][0] = da[0];  // rows 0-7 (digit a), k 4q..4q+3   = group 2q
+        qa[c][1] = db[0];  // rows 8-15 (digit b), same k
+        qa[c][2] = da[1];  // rows 0-7, k 16+4q..               = group 2q+1
+        qa[c][3] = db[1];
+        if constexpr (EX) {
+          qc[c][0] = dc[0];
+          qc[c][1] = dc[1];
+        }
+      }
+  float fac = (amax / 127.0f) * (1.0f / 254.0f) * a.scale * kLog2e;
+  if (nonfinite) fac = __int_as_float(0x7fffffff);  // NaN: the head's output becomes NaN
   float o[NB][2][4];       // O^T accumulators: [block][m-tile][frag]
+#pragma unroll
+  for (int c = 0; c < NB; ++c)
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[c][mt][e] = 0.f;
   float m_run = -INFINITY, l_run = 0.f;
-  // Entry walk: this warp takes units u0 + grp, u0 + grp + GROUPS, ...  It owes a partial for
-  // every batch entry with units in [u0, u1); entries whose units here all belong to the other
-  // group get an empty partial (m = -inf, l = 0, o = 0).
-  int b = -1;                                   // entry of the live accumulators
-  int e_next = find_batch(sm.prefix, B, u0);    // first entry still owed
-  int e_beg = 0, e_end = 0;
   auto write_partial = [&](int e, bool empty) {
     const size_t slot = ((size_t)blockIdx.x + e) * SUBS + slot_sub;
     float lt = empty ? 0.f : l_run;
@@ -401,26 +378,14 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
           *reinterpret_cast<float2*>(po + (size_t)dim * a.n_head) =
               empty ? make_float2(0.f, 0.f) : make_float2(o[c][mt][2 * r], o[c][mt][2 * r + 1]);
         }
-  };
-  auto owe_empty_until = [&](int e_stop) {     // empty partials for entries [e_next, e_stop)
-    if constexpr (GROUPS > 1) {  // with one group every warp sees every unit: nothing owed
-      for (; e_next < e_stop; ++e_next)
-        if (sm.prefix[e_next + 1] > sm.prefix[e_next]) write_partial(e_next, true);
-    }
-  };
-  const float4* wsk = reinterpret_cast<const float4*>(&sm.wsc[warp][0][0][q][0]);  // + 4*c
+  };  const float4* wsk = reinterpret_cast<const float4*>(&sm.wsc[warp][0][0][q][0]);  // + 4*c
   const float4* wsv = reinterpret_cast<const float4*>(&sm.wsc[warp][1][0][q][0]);
   // Inside each 8-token n-tile, MMA column n holds token (n >> 1) + 4 * (n & 1): the V loads of
   // lane (g, q) then read tokens q and 4 + q, whose 544-B rows start in different banks, and
   // the K loads only need their word order swapped on odd columns (swk) to avoid conflicts.
   const int swk = g & 1;
   const int tok_k = (g >> 1) + 4 * (g & 1);  // token loaded for K column g
-
-  // One unit (stage) of the CTA's range; EX: the three-digit query / split-P path.  The two
-  // paths are separate loops over an entry's units, chosen once per entry, so the two-digit
-  // loop carries none of the exact path's code or registers.
-  auto unit_step = [&](auto exact_tag, int u) -> bool {
-    constexpr bool EX = decltype(exact_tag)::value;
+  for (; u < u_stop; u += GROUPS) {
     const int it = u - u0;
     const int buf = it % NS;
     const int bar = it % NBAR;
@@ -615,88 +580,120 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
       }
     }
 
-    // ---- this warp's last unit of the entry in this CTA: write its partial -----------------
-    return true;
-  };
-  for (int u = u0 + grp; u < u1;) {
-    int bu = b < 0 ? e_next : b;
-    while (u >= sm.prefix[bu + 1]) ++bu;
-    if (bu != b) {
-      owe_empty_until(bu);
-      e_next = bu + 1;
-      b = bu;
-      e_beg = a.kv_begin ? a.kv_begin[b] : 0;
-      e_end = a.kv_end[b] + a.end_add;
-      // ---- query digits: q ~= sigma * (d_a + d_b / 254 [+ d_c / 254^2]), sigma = max|q| / 127.
-      //      The third digit (and the f16 hi/lo split of P in PV) is used by warps whose heads
-      //      have max|q| * scale above kTwoDigitMax: outlier channels, as post-norm / RoPE
-      //      queries can have, would otherwise cost the other channels their precision. ------
-      const float* qh = a.q + ((size_t)b * a.n_head + kh * G + g) * HD;
-      float amax = 0.f;
-      bool nonfinite = false;
-#pragma unroll
-      for (int c = 0; c < NB; ++c)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float x = qh[group_dim(c, 2 * q + (i >> 2), i & 3)];
-          amax = fmaxf(amax, fabsf(x));
-          nonfinite |= !isfinite(x);
-        }
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-      nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, 1) != 0;
-      nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, 2) != 0;
-      exact3 = __any_sync(0xffffffffu, amax * a.scale > kTwoDigitMax);
-      const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-#pragma unroll
-      for (int c = 0; c < NB; ++c) {
-        uint32_t da[2] = {0, 0}, db[2] = {0, 0}, dc[2] = {0, 0};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float z = qh[group_dim(c, 2 * q + (i >> 2), i & 3)] * inv;
-          const float ra = fminf(fmaxf(rintf(z), -127.f), 127.f);
-          const float r1 = (z - ra) * 254.0f;        // z - ra is exact
-          const float rb = fminf(fmaxf(rintf(r1), -127.f), 127.f);
-          const float rc =
-              exact3 ? fminf(fmaxf(rintf((r1 - rb) * 254.0f), -127.f), 127.f) : 0.f;
-          const int ia = (ra == ra) ? (int)ra : 0;
-          const int ib = (rb == rb) ? (int)rb : 0;
-          const int ic = (rc == rc) ? (int)rc : 0;
-          da[i >> 2] |= ((uint32_t)ia & 0xffu) << (8 * (i & 3));
-          db[i >> 2] |= ((uint32_t)ib & 0xffu) << (8 * (i & 3));
-          dc[i >> 2] |= ((uint32_t)ic & 0xffu) << (8 * (i & 3));
-        }
-        qa[c][0] = da[0];  // rows 0-7 (digit a), k 4q..4q+3   = group 2q
-        qa[c][1] = db[0];  // rows 8-15 (digit b), same k
-        qa[c][2] = da[1];  // rows 0-7, k 16+4q..               = group 2q+1
-        qa[c][3] = db[1];
-        if (exact3) {
-          qc[c][0] = dc[0];
-          qc[c][1] = dc[1];
-        }
-      }
-      fac = (amax / 127.0f) * (1.0f / 254.0f) * a.scale * kLog2e;
-      if (nonfinite) fac = __int_as_float(0x7fffffff);  // NaN: the head's output becomes NaN
-      m_run = -INFINITY;
-      l_run = 0.f;
-#pragma unroll
-      for (int c = 0; c < NB; ++c)
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) o[c][mt][e] = 0.f;
-    }
-    const int u_stop = min(u1, sm.prefix[b + 1]);
-    if (exact3) {
-      for (; u < u_stop; u += GROUPS)
-        if (!unit_step(std::true_type{}, u)) return;
-    } else {
-      for (; u < u_stop; u += GROUPS)
-        if (!unit_step(std::false_type{}, u)) return;
-    }
-    write_partial(b, false);
   }
-  if constexpr (GROUPS > 1) owe_empty_until(find_batch(sm.prefix, B, u1 - 1) + 1);
+  write_partial(b, false);
+  return true;
+}
+__device__ __noinline__ bool fast_entry_exact(DecodeArgs a, Partials part, int b, int u,
+                                              int u_stop, int u0, int u1, float amax,
+                                              bool nonfinite) {
+  return fast_entry<true>(a, part, b, u, u_stop, u0, u1, amax, nonfinite);
+}
+
+// Warp roles: warp = kv head (bit 0) | 16-token sub-tile (bits 1-2).  Warps only meet at the
+// stage ring: each waits for a stage's bulk copy, and the last warp done with a buffer refills
+// it, so warps drift freely within the ring (no block-wide barrier in the steady state).  At
+// the end of a (batch entry, CTA) segment every warp writes its own (m, l, O) partial; the
+// combine kernel merges them.  Partial slot of warp (kh, sub) in CTA i for entry b:
+// (i + b) * SUBS + sub, heads kh*8 .. kh*8+7, O stored [dim][head].
+__global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(DecodeArgs a,
+                                                                       Partials part) {
+  using namespace fast;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int kh = warp & 1;
+  const int B = a.n_batch;
+  grid_dep_trigger();  // the combine pass may be scheduled as this grid's CTAs retire
+  // Launched to overlap the previous kernel's tail: everything it reads or writes in global
+  // memory (positions, cache, partial slots and the published ranges a previous combine may
+  // still be reading) waits until that kernel has completed.
+  grid_dep_wait();
+
+  // ---- unit prefix over the batch (warp 0: serial per lane chunk + warp scan) -----------
+  if (warp == 0) {
+    const int per = (B + 31) / 32;
+    int run = 0;
+    for (int i = 0; i < per; ++i) {
+      const int bb = lane * per + i;
+      if (bb < B) run += (entry_len(a, bb) + ST - 1) / ST;
+    }
+    int incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int acc = incl - run;
+    for (int i = 0; i < per; ++i) {
+      const int bb = lane * per + i;
+      if (bb < B) {
+        sm.prefix[bb] = acc;
+        acc += (entry_len(a, bb) + ST - 1) / ST;
+      }
+    }
+    if (lane == 31) sm.prefix[B] = incl;
+    __syncwarp();
+    if (blockIdx.x == 0) {  // published for the combine pass: unit prefix and CTA unit ranges
+      for (int i = lane; i <= B; i += 32) part.prefix[i] = sm.prefix[i];
+      const long long Utot = sm.prefix[B];
+      for (int i = lane; i <= (int)gridDim.x; i += 32)
+        part.prefix[B + 1 + i] = (int)((long long)i * Utot / gridDim.x);
+    }
+  }
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(&sm.full[i], 1);
+    for (int i = 0; i < NS; ++i) sm.done[i] = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const long long U = sm.prefix[B];
+  const int u0 = (int)((long long)blockIdx.x * U / gridDim.x);
+  const int u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
+  if (u0 >= u1) return;
+
+  auto issue = [&](int u) {  // unit u -> buffer (u - u0) % NS, barrier (u - u0) % NBAR
+    const UnitInfo ui = unit_info(a, sm.prefix, u);
+    const uint32_t bytes = (uint32_t)ui.ntok * TOKB;
+    const size_t off = ((size_t)ui.s * a.cap + ui.t_start) * TOKB;
+    const int buf = (u - u0) % NS;
+    uint64_t* bar = &sm.full[(u - u0) % NBAR];
+    mbar_arrive_expect_tx(bar, 2 * bytes);
+    bulk_g2s(sm.stage[buf][0], a.k_pool + off, bytes, bar);
+    bulk_g2s(sm.stage[buf][1], a.v_pool + off, bytes, bar);
+  };  if (tid == 0)
+    for (int i = 0; i < NS && u0 + i < u1; ++i) issue(u0 + i);
+
+  static_assert(GROUPS == 1, "every warp takes every unit of the CTA's range");
+  for (int u = u0; u < u1;) {
+    const int b = find_batch(sm.prefix, B, u);
+    const int u_stop = min(u1, sm.prefix[b + 1]);
+    // ---- the warp's heads: max |q| (digit scale) and the choice of the exact path ----------
+    const float* qh = a.q + ((size_t)b * a.n_head + kh * G + g) * HD;
+    float amax = 0.f;
+    bool nonfinite = false;
+#pragma unroll
+    for (int c = 0; c < NB; ++c)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x = qh[group_dim(c, 2 * q + (i >> 2), i & 3)];
+        amax = fmaxf(amax, fabsf(x));
+        nonfinite |= !isfinite(x);
+      }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, 1) != 0;
+    nonfinite |= __shfl_xor_sync(0xffffffffu, (int)nonfinite, 2) != 0;
+    // Heads with outlier channels (max |q| * scale above kTwoDigitMax, as post-norm / RoPE
+    // queries can have) take the three-digit path: two digits relative to the head maximum
+    // would cost the other channels their precision.
+    const bool exact3 = __any_sync(0xffffffffu, amax * a.scale > kTwoDigitMax);
+    const bool ok = exact3 ? fast_entry_exact(a, part, b, u, u_stop, u0, u1, amax, nonfinite)
+                           : fast_entry<false>(a, part, b, u, u_stop, u0, u1, amax, nonfinite);
+    if (!ok) return;
+    u = u_stop;
+  }
 }
 
 // =============================================================================================
