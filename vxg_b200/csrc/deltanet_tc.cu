@@ -553,13 +553,23 @@ __global__ void __launch_bounds__(dntc::THREADS, 1) deltanet_chunk_tc_kernel(Del
       }
       tc::mma_commit(&sm.mma_bar);
     }
-    if (!wait_mma()) break;
-    if (c + 1 < n_chunks) issue_stage_v(c + 1);  // A and T are consumed
-    // ---- W^T -> bf16 hi / lo pairs (over the consumed Z columns); S *= gamma_C -------------------
+    // while the W^T MMAs run (they touch neither): S *= gamma_C, and the next chunk's V rows
+    // are staged over A / T (consumed: T is in its tiles)
     {
-      uint32_t wv[TW], s[SW];
-      tc::tmem_ld16(tl + TM_W + tc0, wv);
+      uint32_t s[SW];
       tc::tmem_ld32(tl + TM_S + sc0, s);
+      tc::wait_ld();
+      const float gc = sm.gam[gb][C - 1];
+#pragma unroll
+      for (int k = 0; k < SW; ++k) s[k] = __float_as_uint(__uint_as_float(s[k]) * gc);
+      tc::tmem_st32(tl + TM_S + sc0, s);
+    }
+    if (c + 1 < n_chunks) issue_stage_v(c + 1);
+    if (!wait_mma()) break;
+    // ---- W^T -> bf16 hi / lo pairs (over the consumed Z columns) ------------------------------
+    {
+      uint32_t wv[TW];
+      tc::tmem_ld16(tl + TM_W + tc0, wv);
       tc::wait_ld();
       uint32_t wh[TW / 2], wl[TW / 2];
 #pragma unroll
@@ -567,10 +577,6 @@ __global__ void __launch_bounds__(dntc::THREADS, 1) deltanet_chunk_tc_kernel(Del
         split_bf16(__uint_as_float(wv[2 * p]), __uint_as_float(wv[2 * p + 1]), wh[p], wl[p]);
       tmem_st8(tl + TM_Z + tc0 / 2, wh);
       tmem_st8(tl + TM_Z + 32 + tc0 / 2, wl);
-      const float gc = sm.gam[gb][C - 1];
-#pragma unroll
-      for (int k = 0; k < SW; ++k) s[k] = __float_as_uint(__uint_as_float(s[k]) * gc);
-      tc::tmem_st32(tl + TM_S + sc0, s);
     }
     sync_for_mma();
     // ---- Y += W^T P^T; S += W^T (e^{L_C - L} K) ---------------------------------------------
@@ -600,14 +606,16 @@ __global__ void __launch_bounds__(dntc::THREADS, 1) deltanet_chunk_tc_kernel(Del
       tc::tmem_ld16(tl + TM_Y + tc0, yv);
       tc::tmem_ld32(tl + TM_S + sc0, s);
       tc::wait_ld();
+      float* op = a.o + (size_t)b * a.o_bs + (size_t)(t0 + tc0) * a.o_ts + (size_t)h * D + row;
+      const int nt = min(TW, a.n_tok - (t0 + tc0));
 #pragma unroll
       for (int k = 0; k < TW; ++k) {
-        const int t = t0 + tc0 + k;
-        if (t < a.n_tok) {
+        if (k < nt) {
           const float o = __uint_as_float(yv[k]);
           bad |= !isfinite(o);
-          a.o[(size_t)b * a.o_bs + (size_t)t * a.o_ts + (size_t)h * a.dv + row] = o;
+          *op = o;
         }
+        op += a.o_ts;
       }
       put_state_planes(s);
     }
