@@ -326,6 +326,23 @@ def test_wide_batch_single_pass_combine(ctx, with_gate):
     pool.close()
 
 
+def test_entry_over_more_slots_than_one_combine_chunk(ctx):
+    """A 32-entry batch (single-level combine) whose last entry holds most of the units, so it
+    is spread over more split CTAs than the combine stages in one chunk (128 slots): the
+    chunks' running maximum is rescaled between them.  1% of K rows x8 make the per-chunk
+    maxima differ."""
+    rng = np.random.default_rng(141)
+    lens = [96] * 31 + [28800]
+    pool, kh, vh, cap = make_pool(ctx, rng, lens, 2, 256, outlier_frac=0.01)
+    seq = np.arange(32, dtype=np.int32)
+    pos = np.array([L - 1 for L in lens], np.int32)
+    q = rng.standard_normal((32, 16, 256)).astype(np.float32)
+    out = pool.decode(seq, pos, q, max_ctx=cap)
+    want = oracle_decode(kh, vh, cap, seq, pos, q, 2, 256)
+    np.testing.assert_allclose(out, want, atol=ATOL, rtol=RTOL)
+    pool.close()
+
+
 def test_misaligned_device_arrays_are_rejected(ctx):
     """Device arrays are accessed with 16-byte vectors and bulk copies: a view that starts one
     float into an allocation is refused on the host, before any launch."""

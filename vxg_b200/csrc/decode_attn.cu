@@ -184,6 +184,7 @@ struct __align__(128) Smem {
 };
 }  // namespace fast
 
+
 size_t fast_smem_bytes() { return sizeof(fast::Smem); }
 
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) {
@@ -590,12 +591,76 @@ __device__ __noinline__ bool fast_entry_exact(DecodeArgs a, Partials part, int b
   return fast_entry<true>(a, part, b, u, u_stop, u0, u1, amax, nonfinite);
 }
 
+// The CTA-wide merge of the staged partials of entry b (all threads; after fast_entry in merge
+// mode): one (m, l, O) slot, sub-tile 0 of the CTA's slots for b, in the usual slot layout.
+// The CTA-wide merge of the partials its warps wrote for its last entry b (all threads, after
+// the unit loop): slots (i + b)*SUBS + sub, sub < SUBS, into one slot (i + b)*SUBS.  The slots
+// were just written by this CTA, so they are read back from L2; every thread issues all its
+// loads before the per-head weights are known, so the two L2 round trips overlap.
+__device__ __forceinline__ void fast_merge_write(const DecodeArgs& a, const Partials& part, int b) {
+  using namespace fast;
+  constexpr int H = NKV * G;
+  constexpr int N2 = HD * H / 2;                    // float2 of O per slot
+  constexpr int IT = (N2 + THREADS - 1) / THREADS;  // per thread
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  float (*wf)[H] = reinterpret_cast<float (*)[H]>(sm.stage);  // [sub][head] weights (idle ring)
+  const int tid = threadIdx.x;
+  const size_t slot = ((size_t)blockIdx.x + b) * SUBS;
+  __syncthreads();  // every warp's partial is written
+  const float2* pi = reinterpret_cast<const float2*>(part.o + slot * H * HD);
+  float2 v[IT][SUBS];
+#pragma unroll
+  for (int k = 0; k < IT; ++k) {
+    const int idx = tid + k * THREADS;
+    if (idx < N2)
+#pragma unroll
+      for (int s = 0; s < SUBS; ++s) v[k][s] = pi[(size_t)s * N2 + idx];
+  }
+  if (tid < H) {
+    float M = -INFINITY, mk[SUBS], lk[SUBS];
+#pragma unroll
+    for (int s = 0; s < SUBS; ++s) {
+      mk[s] = part.m[(slot + s) * H + tid];
+      lk[s] = part.l[(slot + s) * H + tid];
+    }
+#pragma unroll
+    for (int s = 0; s < SUBS; ++s) M = fmaxf(M, mk[s]);
+    float L = 0.f;
+#pragma unroll
+    for (int s = 0; s < SUBS; ++s) {
+      const float f = (mk[s] == -INFINITY || M == -INFINITY) ? 0.f : exp2f(mk[s] - M);
+      wf[s][tid] = f;
+      L = fmaf(lk[s], f, L);
+    }
+    part.m[slot * H + tid] = M;
+    part.l[slot * H + tid] = L;
+  }
+  __syncthreads();
+  float2* po = reinterpret_cast<float2*>(part.o + slot * H * HD);
+#pragma unroll
+  for (int k = 0; k < IT; ++k) {
+    const int idx = tid + k * THREADS;
+    if (idx < N2) {
+      const int h0 = (2 * idx) % H;
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int s = 0; s < SUBS; ++s) {
+        acc.x = fmaf(v[k][s].x, wf[s][h0], acc.x);
+        acc.y = fmaf(v[k][s].y, wf[s][h0 + 1], acc.y);
+      }
+      po[idx] = acc;
+    }
+  }
+}
+
 // Warp roles: warp = kv head (bit 0) | 16-token sub-tile (bits 1-2).  Warps only meet at the
 // stage ring: each waits for a stage's bulk copy, and the last warp done with a buffer refills
 // it, so warps drift freely within the ring (no block-wide barrier in the steady state).  At
-// the end of a (batch entry, CTA) segment every warp writes its own (m, l, O) partial; the
-// combine kernel merges them.  Partial slot of warp (kh, sub) in CTA i for entry b:
-// (i + b) * SUBS + sub, heads kh*8 .. kh*8+7, O stored [dim][head].
+// the end of each (batch entry, CTA) segment every warp writes its own (m, l, O) partial: slot
+// (i + b) * SUBS + sub for warp (kh, sub) of CTA i, heads kh*8 .. kh*8+7, O stored [dim][head].
+// The slots of the CTA's last segment are then merged by the CTA into slot (i + b) * SUBS.  The
+// combine kernel merges the slots.
 __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(DecodeArgs a,
                                                                        Partials part) {
   using namespace fast;
@@ -666,6 +731,8 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
     for (int i = 0; i < NS && u0 + i < u1; ++i) issue(u0 + i);
 
   static_assert(GROUPS == 1, "every warp takes every unit of the CTA's range");
+  bool failed = false;
+  int b_last = 0;
   for (int u = u0; u < u1;) {
     const int b = find_batch(sm.prefix, B, u);
     const int u_stop = min(u1, sm.prefix[b + 1]);
@@ -689,11 +756,17 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
     // queries can have) take the three-digit path: two digits relative to the head maximum
     // would cost the other channels their precision.
     const bool exact3 = __any_sync(0xffffffffu, amax * a.scale > kTwoDigitMax);
-    const bool ok = exact3 ? fast_entry_exact(a, part, b, u, u_stop, u0, u1, amax, nonfinite)
-                           : fast_entry<false>(a, part, b, u, u_stop, u0, u1, amax, nonfinite);
-    if (!ok) return;
+    // A warp that gave up skips the remaining entries but still meets the merge's barriers.
+    if (!failed) {
+      const bool ok =
+          exact3 ? fast_entry_exact(a, part, b, u, u_stop, u0, u1, amax, nonfinite)
+                 : fast_entry<false>(a, part, b, u, u_stop, u0, u1, amax, nonfinite);
+      failed = !ok;
+    }
+    b_last = b;
     u = u_stop;
   }
+  fast_merge_write(a, part, b_last);  // the CTA's last entry: one slot instead of SUBS
 }
 
 // =============================================================================================
@@ -740,8 +813,9 @@ __global__ void __launch_bounds__(256) decode_combine(DecodeArgs a, Partials par
 }
 
 // Fast-path combine.  CTA i of the split pass owned units [i*U/n_cta, (i+1)*U/n_cta) of the unit
-// prefix the split pass published in part.prefix; for each such CTA meeting entry b, slots
-// (i + b)*SUBS + sub hold the partials of its sub-tiles, o stored [dim][head].
+// prefix the split pass published in part.prefix.  For the entry b its range ends in, CTA i
+// merged its partials into slot (i + b)*SUBS; for an entry its range continues past, slots
+// (i + b)*SUBS + sub hold the partials of its sub-tiles.  o stored [dim][head].
 // Grid (entry, 64-dim chunk, slot split z); thread = (dim, slot lane); CTA z merges the slots
 // k = z, z + S, ... of its entry.  With S == 1 it writes the result; otherwise an intermediate
 // (m, l, o) that decode_fast_combine_final merges.
@@ -757,7 +831,7 @@ __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partial
                                                            float* o_out) {
   using namespace fast;
   constexpr int H = NKV * G;
-  constexpr int MAXS = 512 * SUBS;  // every split CTA may meet the entry (grid <= 512)
+  constexpr int MAXS = 512 + SUBS;  // one merged slot per CTA but the last (grid <= 512)
   grid_dep_wait();  // the split pass's partials and published ranges
   grid_dep_trigger();
   const int b = blockIdx.x, z = blockIdx.z;
@@ -769,14 +843,14 @@ __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partial
   __shared__ float s_l[kCombineStage][H];
   __shared__ float s_M[H];
   __shared__ float s_acc[kCombineLanes][kCombineDims][H + 1];
-  __shared__ int s_ilo;
+  __shared__ int s_ilo, s_nm;
   __shared__ int cta_start[512 + 1];  // unit ranges of the split pass's CTAs (n_cta <= 512)
   for (int i = tid; i <= n_cta; i += 256) cta_start[i] = part.prefix[a.n_batch + 1 + i];
   __syncthreads();
   if (tid == 0) {
     if (blockIdx.y == 0 && z == 0 && !entry_valid(a, b)) atomicOr(a.status, kStatusBadIndex);
     const int P0 = part.prefix[b], P1 = part.prefix[b + 1];
-    int n = 0, ilo = 0;
+    int n = 0, ilo = 0, nm = 0;
     if (P1 > P0) {
       // first CTA whose range ends after P0, last CTA whose range starts before P1
       int lo = 0, hi = n_cta - 1;
@@ -793,72 +867,94 @@ __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partial
         if (cta_start[mid] < P1) lo = mid;
         else hi = mid - 1;
       }
-      n = min((lo - ilo + 1) * SUBS, MAXS);
+      // CTAs ilo .. lo-1 end inside this entry, so it was their last and they merged it into
+      // one slot; CTA lo merged it too if its range ends here, else it left SUBS slots
+      nm = lo - ilo;
+      n = min(nm + (cta_start[lo + 1] <= P1 ? 1 : SUBS), MAXS);
     }
     s_ilo = ilo;
+    s_nm = nm;
     s_n = n;
   }
   __syncthreads();
   for (int k = tid; k < s_n; k += 256) {
-    const int i = s_ilo + k / SUBS;
+    const int i = s_ilo + min(k, s_nm), j = max(k - s_nm, 0);
     // a CTA with an empty range (possible only when units < CTAs) wrote no partials
-    s_slot[k] = cta_start[i] < cta_start[i + 1] ? (i + b) * SUBS + k % SUBS : -1;
+    s_slot[k] = cta_start[i] < cta_start[i + 1] ? (i + b) * SUBS + j : -1;
   }
   __syncthreads();
   const int ns = s_n;
   const int nz = ns > z ? (ns - z + S - 1) / S : 0;  // this split's slots: k = z + S*j
-  // running max per head over this split's slots: m staged through shared memory by all
-  // threads (independent loads), then reduced per head
-  if (tid < H) s_M[tid] = -INFINITY;
-  for (int j0 = 0; j0 < nz; j0 += kCombineStage) {
-    const int nk = min(kCombineStage, nz - j0);
-    for (int idx = tid; idx < nk * H; idx += 256) {
-      const int slot = s_slot[z + S * (j0 + idx / H)];
-      s_f[idx / H][idx % H] = slot < 0 ? -INFINITY : part.m[(size_t)slot * H + idx % H];
-    }
-    __syncthreads();
-    if (tid < H) {
-      float M = s_M[tid];
-      for (int k = 0; k < nk; ++k) M = fmaxf(M, s_f[k][tid]);
-      s_M[tid] = M;
-    }
-    __syncthreads();
-  }
+  // One pass over chunks of this split's slots with a running max per head: each chunk's m and
+  // l are staged through shared memory, the weights taken relative to the running max, and
+  // the accumulators rescaled when it grows.  Each thread's first two O rows of a chunk are
+  // loaded before the chunk's m and l are known, so the two round trips overlap.
   float acc[H];
 #pragma unroll
   for (int h = 0; h < H; ++h) acc[h] = 0.f;
   float Lp = 0.f;
+  if (tid < H) s_M[tid] = -INFINITY;
+  auto o_row = [&](int k, int j0) -> const float4* {
+    const int slot = k < min(kCombineStage, nz - j0) ? s_slot[z + S * (j0 + k)] : -1;
+    return slot < 0 ? nullptr
+                    : reinterpret_cast<const float4*>(part.o + ((size_t)slot * HD + d) * H);
+  };
   for (int j0 = 0; j0 < nz; j0 += kCombineStage) {
     const int nk = min(kCombineStage, nz - j0);
+    float4 x0[H / 4], x1[H / 4];
+    const float4* r0 = o_row(sl, j0);
+    const float4* r1 = o_row(sl + kCombineLanes, j0);
+#pragma unroll
+    for (int v = 0; v < H / 4; ++v) {
+      x0[v] = r0 ? r0[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+      x1[v] = r1 ? r1[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     for (int idx = tid; idx < nk * H; idx += 256) {
       const int k = idx / H, h = idx % H;
       const int slot = s_slot[z + S * (j0 + k)];
-      if (slot < 0) {
-        s_f[k][h] = 0.f;
-        s_l[k][h] = 0.f;
-        continue;
-      }
-      const size_t sl2 = (size_t)slot * H + h;
-      const float mk = part.m[sl2], M = s_M[h];
-      s_f[k][h] = (mk == -INFINITY || M == -INFINITY) ? 0.f : exp2f(mk - M);
-      s_l[k][h] = part.l[sl2];
+      s_f[k][h] = slot < 0 ? -INFINITY : part.m[(size_t)slot * H + h];
+      s_l[k][h] = slot < 0 ? 0.f : part.l[(size_t)slot * H + h];
     }
     __syncthreads();
-    if (tid < H)
-      for (int k = 0; k < nk; ++k) Lp = fmaf(s_l[k][tid], s_f[k][tid], Lp);
-#pragma unroll 2
-    for (int k = sl; k < nk; k += kCombineLanes) {
-      const int slot = s_slot[z + S * (j0 + k)];
-      if (slot < 0) continue;
-      const float4* orow = reinterpret_cast<const float4*>(part.o + ((size_t)slot * HD + d) * H);
+    if (tid < H) {
+      const float Mo = s_M[tid];
+      float M = Mo;
+      for (int k = 0; k < nk; ++k) M = fmaxf(M, s_f[k][tid]);
+      const float r = Mo == -INFINITY ? 0.f : exp2f(Mo - M);  // Mo <= M
+      Lp *= r;
+      for (int k = 0; k < nk; ++k) {
+        const float mk = s_f[k][tid];
+        const float f = (mk == -INFINITY || M == -INFINITY) ? 0.f : exp2f(mk - M);
+        s_f[k][tid] = f;
+        Lp = fmaf(s_l[k][tid], f, Lp);
+      }
+      s_M[tid] = M;
+      s_l[0][tid] = r;  // this chunk's rescale of the accumulators (s_l is consumed)
+    }
+    __syncthreads();
+    if (j0 > 0) {
+#pragma unroll
+      for (int h = 0; h < H; ++h) acc[h] *= s_l[0][h];
+    }
+    auto fma_row = [&](const float4 (&x)[H / 4], int k) {
 #pragma unroll
       for (int v = 0; v < H / 4; ++v) {
-        const float4 x = orow[v];
-        acc[4 * v] = fmaf(x.x, s_f[k][4 * v], acc[4 * v]);
-        acc[4 * v + 1] = fmaf(x.y, s_f[k][4 * v + 1], acc[4 * v + 1]);
-        acc[4 * v + 2] = fmaf(x.z, s_f[k][4 * v + 2], acc[4 * v + 2]);
-        acc[4 * v + 3] = fmaf(x.w, s_f[k][4 * v + 3], acc[4 * v + 3]);
+        acc[4 * v] = fmaf(x[v].x, s_f[k][4 * v], acc[4 * v]);
+        acc[4 * v + 1] = fmaf(x[v].y, s_f[k][4 * v + 1], acc[4 * v + 1]);
+        acc[4 * v + 2] = fmaf(x[v].z, s_f[k][4 * v + 2], acc[4 * v + 2]);
+        acc[4 * v + 3] = fmaf(x[v].w, s_f[k][4 * v + 3], acc[4 * v + 3]);
       }
+    };
+    if (r0) fma_row(x0, sl);
+    if (r1) fma_row(x1, sl + kCombineLanes);
+#pragma unroll 2
+    for (int k = sl + 2 * kCombineLanes; k < nk; k += kCombineLanes) {
+      const float4* rk = o_row(k, j0);
+      if (!rk) continue;
+      float4 x[H / 4];
+#pragma unroll
+      for (int v = 0; v < H / 4; ++v) x[v] = rk[v];
+      fma_row(x, k);
     }
     __syncthreads();
   }
@@ -915,6 +1011,11 @@ __global__ void __launch_bounds__(256) decode_fast_combine_final(DecodeArgs a, P
   const float* il = im + (size_t)a.n_batch * S * H;
   const float* io = il + (size_t)a.n_batch * S * H;
   __shared__ float s_m[kCombineSplitMax], s_l[kCombineSplitMax];
+  // every intermediate of this (entry, head, dim) is loaded at once, beside m and l
+  float ov[kCombineSplitMax];
+#pragma unroll
+  for (int z = 0; z < kCombineSplitMax; ++z)
+    ov[z] = z < S ? io[(((size_t)b * S + z) * H + h) * HD + d] : 0.f;
   if (d < S) {
     s_m[d] = im[((size_t)b * S + d) * H + h];
     s_l[d] = il[((size_t)b * S + d) * H + h];
@@ -924,12 +1025,13 @@ __global__ void __launch_bounds__(256) decode_fast_combine_final(DecodeArgs a, P
   for (int z = 0; z < S; ++z) M = fmaxf(M, s_m[z]);
   float L = 0.f, O = 0.f;
   if (M != -INFINITY)
-#pragma unroll 4
-    for (int z = 0; z < S; ++z) {
+#pragma unroll
+    for (int z = 0; z < kCombineSplitMax; ++z) {
+      if (z >= S) break;
       const float mz = s_m[z];
       const float f = mz == -INFINITY ? 0.f : exp2f(mz - M);
       L = fmaf(s_l[z], f, L);
-      O = fmaf(io[(((size_t)b * S + z) * H + h) * HD + d], f, O);
+      O = fmaf(ov[z], f, O);
     }
   const size_t oi = ((size_t)b * H + h) * HD + d;
   if (m_out) {
