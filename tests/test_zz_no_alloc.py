@@ -77,7 +77,7 @@ def _scratch_bytes_16_2_256(n, sm_count):
     splits = max(1, min(32, -(-128 // (4 * n))))
     if splits > 1:
         floats += n * splits * 16 * 258
-    return 4 * (floats + n + grid + 64)
+    return 4 * (1056 + floats + n + grid + 64)  # + the split pass's state (rates per CTA)
 
 
 def _largest_batch(sm_count):

@@ -331,9 +331,14 @@ vxg::DecodeArgs decode_args(Kv& kv, uint32_t n_batch, uint32_t n_head, const int
   return a;
 }
 
-vxg::Partials carve_partials(Ctx& c, const vxg::DecodeArgs& a) {
+// The split-KV scratch of the context; a new allocation starts with zeroed split-pass state
+// (cleared on the stream the call's kernels use).
+vxg::Partials carve_partials(Ctx& c, const vxg::DecodeArgs& a, cudaStream_t st) {
   const size_t floats = vxg::decode_partial_floats(a, c.sm_count);
+  const size_t had = c.part.n;
   c.part.reserve(floats * sizeof(float), "cudaMalloc partials");
+  if (c.part.n != had)
+    check(cudaMemsetAsync(c.part.p, 0, sizeof(vxg::FastState), st), "partials state reset");
   return vxg::carve_partials(static_cast<float*>(c.part.p), a, c.sm_count);
 }
 
@@ -758,7 +763,7 @@ int vxg_attn_cuda_q8_decode(void* ctx, void* h, uint32_t n_batch, uint32_t n_hea
             "q8_append launch");
     vxg::DecodeArgs a = decode_args(kv, n_batch, n_head, seq_ids, nullptr, pos, 1, q, scale,
                                     max_ctx, c.d_status);
-    vxg::Partials p = carve_partials(c, a);
+    vxg::Partials p = carve_partials(c, a, st);
     cudaEvent_t e0, e1;
     record_timing(c, &e0, &e1);
     check(vxg::launch_decode(a, p, q_gate, out, c.sm_count, c.force_generic, st, e0, e1),
@@ -821,7 +826,7 @@ int vxg_attn_cuda_q8_decode_host_async(void* ctx, void* h, uint32_t n_batch, uin
             "q8_append launch");
     vxg::DecodeArgs a = decode_args(kv, n_batch, n_head, dseq, nullptr, dpos, 1, dq, scale,
                                     max_ctx, dst);
-    vxg::Partials p = carve_partials(c, a);
+    vxg::Partials p = carve_partials(c, a, c.stream);
     cudaEvent_t e0, e1;
     record_timing(c, &e0, &e1);
     check(vxg::launch_decode(a, p, dg, dout, c.sm_count, c.force_generic, c.stream, e0, e1),
@@ -998,7 +1003,7 @@ int vxg_attn_cuda_f32_decode(void* ctx, void* h, uint32_t n_batch, uint32_t n_he
             "f32 append launch");
     vxg::DecodeArgs a = decode_args(kv, n_batch, n_head, seq_ids, nullptr, pos, 1, q, scale,
                                     max_ctx, c.d_status);
-    vxg::Partials p = carve_partials(c, a);
+    vxg::Partials p = carve_partials(c, a, st);
     cudaEvent_t e0, e1;
     record_timing(c, &e0, &e1);
     check(vxg::launch_decode(a, p, q_gate, out, c.sm_count, 1, st, e0, e1), "decode launch");
@@ -1039,7 +1044,7 @@ int vxg_attn_cuda_q8_decode_partial(void* ctx, void* h, uint32_t n_batch, uint32
     sg.upload();
     vxg::DecodeArgs a = decode_args(kv, n_batch, n_head, seq_ids, kv_begin, kv_end, 0, q, scale,
                                     max_ctx, c.d_status);
-    vxg::Partials p = carve_partials(c, a);
+    vxg::Partials p = carve_partials(c, a, st);
     cudaEvent_t e0, e1;
     record_timing(c, &e0, &e1);
     check(vxg::launch_decode_partial(a, p, m, l, o, c.sm_count, c.force_generic, st, e0, e1),
@@ -1245,7 +1250,7 @@ int vxg_attn_cuda_step_full_gqa_q8(void* ctx, void* h, uint32_t seq, const float
     const float scale = 1.0f / sqrtf((float)head_dim);
     vxg::DecodeArgs a = decode_args(kv, 1, n_head, d_seq, nullptr, d_pos, 1, dq, scale, pos + 1,
                                     c.d_status);
-    vxg::Partials p = carve_partials(c, a);
+    vxg::Partials p = carve_partials(c, a, st);
     float* dout = reinterpret_cast<float*>(base + o_out);
     check(vxg::launch_decode(a, p, dg, dout, c.sm_count, c.force_generic, st, nullptr, nullptr),
           "decode launch");
@@ -1326,7 +1331,7 @@ int vxg_attn_cuda_step_full_gqa(void* ctx, void* h, uint32_t seq, const float* q
     const float scale = 1.0f / sqrtf((float)head_dim);
     vxg::DecodeArgs a = decode_args(kv, 1, n_head, d_seq, nullptr, d_pos, 1, dq, scale, pos + 1,
                                     c.d_status);
-    vxg::Partials p = carve_partials(c, a);
+    vxg::Partials p = carve_partials(c, a, st);
     float* dout = reinterpret_cast<float*>(base + o_out);
     check(vxg::launch_decode(a, p, dg, dout, c.sm_count, 1, st, nullptr, nullptr),
           "decode launch");

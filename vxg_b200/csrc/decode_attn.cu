@@ -179,6 +179,10 @@ struct __align__(128) Smem {
   uint8_t stage[NS][2][STB];       // [buf][K, V][token][kv head][block] raw KvQ8Blocks
   float wsc[WARPS][2][NB][4][4];   // per-warp K/V scales: [block][q][tokens 2q,2q+1,2q+8,2q+9]
   int prefix[MAXB + 1];            // units before batch entry b
+  int range[2];                    // this CTA's unit range
+  float rate_old;                  // its range's rate in the last call (0: none)
+  int cur;                         // the current rate buffer
+  unsigned long long t_first;      // arrival of the CTA's first stage (globaltimer ns)
   unsigned done[NS];               // warps finished with each buffer
   uint64_t full[NBAR];
 };
@@ -402,6 +406,7 @@ __device__ __forceinline__ bool fast_entry(const DecodeArgs& a, const Partials& 
         if (u + k < u1) mbar_wait(&sm.full[(it + k) % NBAR], (uint32_t)((it + k) / NBAR) & 1u, kWaitNs);
       return false;
     }
+    if (it == 0 && threadIdx.x == 0) sm.t_first = globaltimer_ns();  // the range's rate clock
     const uint8_t* kst = sm.stage[buf][0];
     const uint8_t* vst = sm.stage[buf][1];
 
@@ -671,16 +676,101 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
   const int kh = warp & 1;
   const int B = a.n_batch;
   grid_dep_trigger();  // the combine pass may be scheduled as this grid's CTAs retire
+  // ---- CTA unit ranges: the U units in proportion to the rates the CTAs' ranges streamed at
+  // in the last call (clamped to [1/2, 2] x their mean; equal shares when a rate is missing).
+  // Ranges that cross batch entries pay per-entry set-up and partial writes and run
+  // persistently slower (up to ~14% per unit in a 64-entry batch), so equal shares leave the
+  // kernel waiting for its slowest CTAs.  A single entry has no such ranges: it takes equal
+  // shares and keeps no rates (the batch size is the same for every CTA, and every CTA of a
+  // weighted call counts in).  Every CTA computes the boundaries
+  // identically from the same rates.  Before the dependency wait (overlapping the previous
+  // kernel's tail): the current rate buffer and its clamped prefix sums (the previous split
+  // pass, which wrote them and flipped `cur`, completed before the combine pass that let this
+  // grid start), and L2 prefetches of the entries' positions (no values are taken before the
+  // wait).  Lane l of warp 0 holds ranges 16l .. 16l+15.
+  const int nc = gridDim.x;  // <= 512
+  const bool weighted = B >= 2;
+  float w[16];               // clamped weights
+  float wp = 0.f, wt = 1.f, rate_old = 0.f;
+  int cur = 0;
+  if (warp == 0 && weighted) {
+    auto weights = [&](const float* rates, float (&w)[16], float& wp, float& wt, float& old) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {  // (entries past nc are read, then ignored)
+        const float4 x = reinterpret_cast<const float4*>(rates)[lane * 4 + j];
+        w[4 * j] = x.x, w[4 * j + 1] = x.y, w[4 * j + 2] = x.z, w[4 * j + 3] = x.w;
+      }
+      float wsum = 0.f;
+      bool have = true;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int i = lane * 16 + j;
+        const bool ok = w[j] > 0.f && w[j] < 1e30f;
+        if (i < nc) {
+          have &= ok;
+          wsum += w[j];
+        }
+        if (i == (int)blockIdx.x) old = ok ? w[j] : 0.f;
+      }
+      have = __all_sync(0xffffffffu, have);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+      const float mean = wsum / (float)nc;
+      float run_w = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int i = lane * 16 + j;
+        w[j] = i >= nc ? 0.f : have ? fminf(fmaxf(w[j], 0.5f * mean), 2.0f * mean) : 1.0f;
+        run_w += w[j];
+      }
+      float incl_w = run_w;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(0xffffffffu, incl_w, o);
+        if (lane >= o) incl_w += v;
+      }
+      wt = __shfl_sync(0xffffffffu, incl_w, 31);
+      wp = __shfl_up_sync(0xffffffffu, incl_w, 1);
+      if (lane == 0) wp = 0.f;
+    };
+    for (int bb = lane; bb < B; bb += 32) {
+      prefetch_l2(a.seq_ids + bb);
+      prefetch_l2(a.kv_end + bb);
+      if (a.kv_begin) prefetch_l2(a.kv_begin + bb);
+    }
+    cur = part.state->cur & 1;
+    weights(part.state->rate[cur], w, wp, wt, rate_old);
+    // the sums are taken here, before the wait: their loads' latency overlaps the previous
+    // kernel instead of following the wait
+    asm volatile("" ::"f"(wt), "f"(wp));
+  } else if (warp == 0) {  // equal shares
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] = lane * 16 + j < nc ? 1.0f : 0.0f;
+    wp = (float)min(lane * 16, nc);
+    wt = (float)nc;
+  }
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(&sm.full[i], 1);
+    for (int i = 0; i < NS; ++i) sm.done[i] = 0;
+    fence_mbar_init();
+  }
   // Launched to overlap the previous kernel's tail: everything it reads or writes in global
-  // memory (positions, cache, partial slots and the published ranges a previous combine may
-  // still be reading) waits until that kernel has completed.
+  // memory (positions, cache, partial slots, the current rate buffer and the published ranges
+  // a previous combine may still be reading) waits until that kernel has completed.
   grid_dep_wait();
 
   // ---- unit prefix over the batch (warp 0: serial per lane chunk + warp scan) -----------
   if (warp == 0) {
     const int per = (B + 31) / 32;
+    int lc[4];  // lengths of the lane's first four entries
     int run = 0;
-    for (int i = 0; i < per; ++i) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int bb = lane * per + i;
+      lc[i] = i < per && bb < B ? entry_len(a, bb) : 0;
+      run += (lc[i] + ST - 1) / ST;
+    }
+    for (int i = 4; i < per; ++i) {
       const int bb = lane * per + i;
       if (bb < B) run += (entry_len(a, bb) + ST - 1) / ST;
     }
@@ -691,7 +781,15 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
       if (lane >= o) incl += v;
     }
     int acc = incl - run;
-    for (int i = 0; i < per; ++i) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int bb = lane * per + i;
+      if (i < per && bb < B) {
+        sm.prefix[bb] = acc;
+        acc += (lc[i] + ST - 1) / ST;
+      }
+    }
+    for (int i = 4; i < per; ++i) {
       const int bb = lane * per + i;
       if (bb < B) {
         sm.prefix[bb] = acc;
@@ -699,24 +797,56 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
       }
     }
     if (lane == 31) sm.prefix[B] = incl;
-    __syncwarp();
-    if (blockIdx.x == 0) {  // published for the combine pass: unit prefix and CTA unit ranges
-      for (int i = lane; i <= B; i += 32) part.prefix[i] = sm.prefix[i];
-      const long long Utot = sm.prefix[B];
-      for (int i = lane; i <= (int)gridDim.x; i += 32)
-        part.prefix[B + 1 + i] = (int)((long long)i * Utot / gridDim.x);
+    // boundary i = floor(U * W_i / W) with W_i the weights before range i: monotone in i
+    // (rounded products and quotients of positive floats are), the same in every CTA.  CTA 0
+    // computes them all (published for the combine pass), the others their own two.
+    const int Utot = __shfl_sync(0xffffffffu, incl, 31);  // units of the batch
+    const float uw = (float)Utot / wt;
+    auto bound = [&](int i, float wpi) {
+      return i == 0 ? 0 : min(Utot, (int)fminf(wpi * uw, (float)Utot));
+    };
+    const int lo = (int)blockIdx.x;
+    if (lo == 0 || lane == lo / 16 || lane == (lo + 1) / 16) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int i = lane * 16 + j;
+        if (i < nc) {
+          if (lo == 0) part.prefix[B + 1 + i] = bound(i, wp);  // published for the combine
+          if (i == lo) sm.range[0] = bound(i, wp);
+          if (i == lo + 1) sm.range[1] = bound(i, wp);
+        }
+        wp += w[j];
+      }
     }
-  }
-  if (tid == 0) {
-    for (int i = 0; i < NBAR; ++i) mbar_init(&sm.full[i], 1);
-    for (int i = 0; i < NS; ++i) sm.done[i] = 0;
-    fence_mbar_init();
+    if (lane == (int)blockIdx.x / 16) sm.rate_old = rate_old;
+    if (lane == 0) {
+      if (lo + 1 == nc) sm.range[1] = Utot;
+      if (lo == 0) part.prefix[B + 1 + nc] = Utot;
+      sm.cur = cur;
+    }
+    __syncwarp();
+    if (blockIdx.x == 0)  // published for the combine pass
+      for (int i = lane; i <= B; i += 32) part.prefix[i] = sm.prefix[i];
   }
   __syncthreads();
-  const long long U = sm.prefix[B];
-  const int u0 = (int)((long long)blockIdx.x * U / gridDim.x);
-  const int u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
-  if (u0 >= u1) return;
+  const int u0 = sm.range[0], u1 = sm.range[1];
+  // this range's rate for the next call (units per microsecond, smoothed over calls); none
+  // from a range too short to measure, which makes the next call take equal shares
+  auto put_rate = [&](float measured) {
+    const float old = sm.rate_old;
+    FastState* fs = part.state;
+    fs->rate[sm.cur ^ 1][blockIdx.x] =
+        measured <= 0.f ? 0.f : old > 0.f ? 0.5f * (old + measured) : measured;
+    // the last CTA to finish (every CTA has read `cur` by then) makes these rates current
+    if (atomicAdd(&fs->done, 1u) == (unsigned)gridDim.x - 1) {
+      fs->done = 0;
+      fs->cur = sm.cur ^ 1;
+    }
+  };
+  if (u0 >= u1) {
+    if (weighted && tid == 0) put_rate(0.f);
+    return;
+  }
 
   auto issue = [&](int u) {  // unit u -> buffer (u - u0) % NS, barrier (u - u0) % NBAR
     const UnitInfo ui = unit_info(a, sm.prefix, u);
@@ -765,6 +895,10 @@ __global__ void __launch_bounds__(fast::THREADS, fast::CPS) decode_fast_split(De
     }
     b_last = b;
     u = u_stop;
+  }
+  if (weighted && tid == 0) {  // streaming rate: units after the first over the time since
+    const float us = (float)(globaltimer_ns() - sm.t_first) * 1e-3f;
+    put_rate(u1 - u0 >= 8 && us > 0.f ? (float)(u1 - u0 - 1) / us : 0.f);
   }
   fast_merge_write(a, part, b_last);  // the CTA's last entry: one slot instead of SUBS
 }
@@ -1121,7 +1255,7 @@ size_t decode_partial_floats(const DecodeArgs& a, int sm_count) {
   size_t slots;
   if (fast_applies(a)) slots = ((size_t)fast_grid(sm_count) + a.n_batch) * fast::SUBS;
   else slots = (size_t)a.n_batch * generic_max_split(a);
-  size_t f = slots * a.n_head * (2 + (size_t)a.nb * 32);
+  size_t f = kFastStateFloats + slots * a.n_head * (2 + (size_t)a.nb * 32);
   const int S = fast_applies(a) ? combine_splits(a) : 1;
   if (S > 1) f += (size_t)a.n_batch * S * a.n_head * (2 + fast::HD);
   if (fast_applies(a)) f += (size_t)a.n_batch + fast_grid(sm_count) + 64;  // prefix + CTA ranges
@@ -1133,6 +1267,8 @@ Partials carve_partials(float* base, const DecodeArgs& a, int sm_count) {
   if (fast_applies(a)) slots = ((size_t)fast_grid(sm_count) + a.n_batch) * fast::SUBS;
   else slots = (size_t)a.n_batch * generic_max_split(a);
   Partials p;
+  p.state = reinterpret_cast<FastState*>(base);
+  base += kFastStateFloats;
   p.m = base;
   p.l = base + slots * a.n_head;
   p.o = base + 2 * slots * a.n_head;

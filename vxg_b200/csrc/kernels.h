@@ -62,7 +62,22 @@ struct DecodeArgs {
 };
 
 // Partial (m, l, o) buffers for the split-KV pass: m, l in log2 units, o unnormalised.
+// State of the fast split pass that outlives a call, at the front of the split-KV scratch
+// (zero when the scratch is new): the measured units per microsecond of each CTA's range in the
+// last call, in two buffers.  The split pass reads buffer `cur` to size its CTAs' unit ranges
+// and writes the other; the last of its CTAs to finish (counted in `done`) flips `cur`, after
+// every CTA has read it.  Every CTA of one call thus reads the same rates, and any rates give
+// a valid partition of the units.
+struct FastState {
+  int cur;
+  unsigned done;
+  int pad[30];
+  float rate[2][512];
+};
+constexpr size_t kFastStateFloats = sizeof(FastState) / sizeof(float);
+
 struct Partials {
+  FastState* state;  // the split pass's cross-call state (front of the scratch)
   float* m;   // [n_slot][n_head]
   float* l;   // [n_slot][n_head]
   float* o;   // [n_slot][n_head][hd]
