@@ -160,8 +160,9 @@ class LongContextDecoder:
         dev = torch.device("cuda", torch.cuda.current_device())
         self._seq = torch.zeros(1, dtype=torch.int32, device=dev)
         self._begin = torch.zeros(1, dtype=torch.int32, device=dev)
-        self._end = torch.zeros(1, dtype=torch.int32, device=dev)
-        self._pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        # one-element views of a constant 0 .. span table stand for this step's local position
+        # and length: no kernel to set them (a captured step replays with its own views)
+        self._ar = torch.arange(self.range.span + 1, dtype=torch.int32, device=dev)
         per = n_head * (head_dim + 2)
         self._send = torch.empty(per, dtype=torch.float32, device=dev)
         self._recv = torch.empty(world * per, dtype=torch.float32, device=dev)
@@ -185,11 +186,11 @@ class LongContextDecoder:
         from .attn import lse_combine_packed
         r = self.range
         if r.owner(pos) == r.rank:
-            self._pos.fill_(r.local_pos(pos))
-            self.pool.append(self._seq, self._pos, k_new.reshape(1, 1, -1, self.head_dim),
+            lp = r.local_pos(pos)
+            self.pool.append(self._seq, self._ar[lp:lp + 1], k_new.reshape(1, 1, -1, self.head_dim),
                              v_new.reshape(1, 1, -1, self.head_dim))
-        self._end.fill_(r.local_len(pos + 1))
-        self.pool.decode_partial(self._seq, self._begin, self._end,
+        le = r.local_len(pos + 1)
+        self.pool.decode_partial(self._seq, self._begin, self._ar[le:le + 1],
                                  q.reshape(1, self.n_head, self.head_dim), scale=scale,
                                  out=(self._m, self._l, self._o))
         if self.peer is not None:
