@@ -1140,6 +1140,7 @@ __global__ void __launch_bounds__(256) decode_fast_combine_final(DecodeArgs a, P
   using namespace fast;
   constexpr int H = NKV * G;
   grid_dep_wait();  // the slot-split combine's intermediates
+  grid_dep_trigger();
   const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const float* im = part.inter;
   const float* il = im + (size_t)a.n_batch * S * H;

@@ -5,7 +5,8 @@
 //                                  rank, double-buffered by step parity
 //   uint32   flag[2][world]        step number whose partials rank r has stored in slot r
 //   uint32   step                  steps pushed by this rank so far
-// A step is two launches on the caller's stream.  peer_push_kernel (one CTA) stores this rank's
+// A step is two launches on the caller's stream (programmatic dependent launches: each is
+// scheduled while the kernel before it runs and waits for that grid to complete first).  peer_push_kernel (one CTA) stores this rank's
 // packed partials into slot `rank` of every rank's buffer (its own included) with plain stores
 // through the IPC mappings, fences at system scope, then raises flag[p][rank] = step in every
 // buffer with a system-scope release store.  peer_combine_kernel (one CTA per row) waits,
@@ -18,6 +19,7 @@
 // Peer memory is only written with ordinary stores (no TMA).
 #include <cuda_runtime.h>
 
+#include "common.cuh"
 #include "kernels.h"
 
 namespace vxg {
@@ -49,6 +51,8 @@ __global__ void __launch_bounds__(512) peer_push_kernel(const float* __restrict_
                                                         PeerTable peers, int world, int rank,
                                                         uint32_t* local_step) {
   __shared__ uint32_t s_step;
+  grid_dep_wait();     // the partials (and the step counter) written before this launch
+  grid_dep_trigger();  // the combine may be scheduled now; it waits for this grid to complete
   if (threadIdx.x == 0) s_step = ld_volatile(local_step) + 1;
   __syncthreads();
   const uint32_t step = s_step;
@@ -83,6 +87,7 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(const float* buf, int
   const uint32_t* local_step = flags + 2 * world;
   __shared__ int s_ok;
   __shared__ uint32_t s_step;
+  grid_dep_wait();  // this rank's push has completed before the flags are polled
   if (threadIdx.x == 0) {
     const uint32_t step = ld_volatile(local_step);
     const int p = step & 1;
@@ -137,16 +142,18 @@ cudaError_t launch_peer_push(const float* send, int per, const PeerTable& peers,
                              int rank, float* local_buf, cudaStream_t st) {
   uint32_t* local_step =
       reinterpret_cast<uint32_t*>(local_buf + (size_t)2 * world * per) + 2 * world;
-  peer_push_kernel<<<1, 512, 0, st>>>(send, per, peers, world, rank, local_step);
-  return cudaGetLastError();
+  // programmatic dependent launches: the launch overlaps the previous kernel; each kernel
+  // waits for its predecessor's grid to complete before it touches memory
+  return launch_dependent(peer_push_kernel, dim3(1), dim3(512), 0, st, send, per, peers, world,
+                          rank, local_step);
 }
 
 cudaError_t launch_peer_combine(const float* local_buf, int world, int n_rows, int hd,
                                 const float* gate, float* out, uint32_t* status,
                                 cudaStream_t st) {
   if (n_rows == 0) return cudaSuccess;
-  peer_combine_kernel<<<n_rows, 256, 0, st>>>(local_buf, world, n_rows, hd, gate, out, status);
-  return cudaGetLastError();
+  return launch_dependent(peer_combine_kernel, dim3(n_rows), dim3(256), 0, st, local_buf, world,
+                          n_rows, hd, gate, out, status);
 }
 
 }  // namespace vxg
