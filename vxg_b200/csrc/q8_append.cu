@@ -47,6 +47,10 @@ __global__ void __launch_bounds__(256) q8_append_kernel(const int32_t* __restric
                                                          int cap, int n_kv, int nb, bool vec,
                                                          uint32_t* status) {
   grid_dep_trigger();  // a decode pass launched after this may start its set-up now
+  // Launched as a programmatic dependent: the launch overlaps the previous kernel's tail, and
+  // nothing is read (positions, inputs) or written (the cache a previous pass may still read)
+  // before that kernel has completed.
+  grid_dep_wait();
   const long long blk_id = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
   const int sub = threadIdx.x & 7;
   const int per_tok = n_kv * nb;                 // blocks per token in one cache
@@ -102,10 +106,9 @@ cudaError_t launch_q8_append(const int32_t* seq_ids, const int32_t* pos, const f
   const int threads = 256;
   const long long blocks = (n_blk * 8 + threads - 1) / threads;
   const bool vec = ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15u) == 0;
-  q8_append_kernel<float><<<(unsigned)blocks, threads, 0, stream>>>(
-      seq_ids, pos, k_new, v_new, k_pool, v_pool, n_batch, n_tok, n_seq, cap, n_kv, nb, vec,
-      status);
-  return cudaGetLastError();
+  return launch_dependent(q8_append_kernel<float>, dim3((unsigned)blocks), dim3(threads), 0,
+                          stream, seq_ids, pos, k_new, v_new, k_pool, v_pool, n_batch, n_tok,
+                          n_seq, cap, n_kv, nb, vec, status);
 }
 
 cudaError_t launch_q8_append_bf16(const int32_t* seq_ids, const int32_t* pos, const void* k_new,
@@ -117,11 +120,10 @@ cudaError_t launch_q8_append_bf16(const int32_t* seq_ids, const int32_t* pos, co
   const int threads = 256;
   const long long blocks = (n_blk * 8 + threads - 1) / threads;
   const bool vec = ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 7u) == 0;
-  q8_append_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, stream>>>(
-      seq_ids, pos, static_cast<const __nv_bfloat16*>(k_new),
-      static_cast<const __nv_bfloat16*>(v_new), k_pool, v_pool, n_batch, n_tok, n_seq, cap, n_kv,
-      nb, vec, status);
-  return cudaGetLastError();
+  return launch_dependent(q8_append_kernel<__nv_bfloat16>, dim3((unsigned)blocks), dim3(threads),
+                          0, stream, seq_ids, pos, static_cast<const __nv_bfloat16*>(k_new),
+                          static_cast<const __nv_bfloat16*>(v_new), k_pool, v_pool, n_batch,
+                          n_tok, n_seq, cap, n_kv, nb, vec, status);
 }
 
 // fp32 pools: one thread per 4 floats of one (batch entry, token) row of K and of V.
