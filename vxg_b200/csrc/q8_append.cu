@@ -132,8 +132,9 @@ __global__ void __launch_bounds__(256) q8_append_kernel(const int32_t* __restric
   uint32_t code[kVals];
 #pragma unroll
   for (int i = 0; i < kVals; ++i) {
-    const float rq = rintf(x[i] * inv);
-    const int qi = (rq == rq) ? (int)fminf(fmaxf(rq, -127.0f), 127.0f) : 0;
+    // round half to even (a NaN product becomes 0, as the reference's cast), then clamp to
+    // +-127: a scale that rounded down to a binary16 subnormal can put |x * inv| above 127.5
+    const int qi = max(-127, min(127, __float2int_rn(x[i] * inv)));
     code[i] = (uint32_t)qi & 0xFFu;
   }
   uint8_t* dst = (which ? v_pool : k_pool) + (((size_t)s * cap + p) * per_tok + blk) * kBlk;
