@@ -501,15 +501,16 @@ def measure_long(args, world, rank, local, ctx, K, W, check=False):
     N GPUs: the KV range is split across ranks (vxg_b200.dist.LongContextDecoder): append on the
     owning rank, per-rank split-KV partial, exchange of (m, l, o) (NVLink peer memory or one
     NCCL all-gather), LSE combine.  A step is ~0.1 ms of device work, so on N GPUs the K timed
-    steps are captured once into a CUDA graph and replayed; the split time per launch comes from
-    an eager pass of K further steps.  With ``check``, the first step's merged output is compared
+    steps are captured once into a CUDA graph and replayed, after one untimed step (a graph of
+    its own, replayed first) that absorbs the skew between the ranks' replay launches; the split
+    time per launch comes from an eager pass of K further steps.  With ``check``, the first step's merged output is compared
     on rank 0 with a one-GPU decode of the same whole cache, before anything is timed."""
     import torch
     import torch.distributed as dist
     import vxg_b200
     from vxg_b200 import workloads as wl
     L = 262144
-    n_in = 1 + W + 2 * K
+    n_in = 2 + W + 2 * K
     cap = L + n_in + 8
     q, kn, vn = wl.decode_step_inputs_device(1, n_in, seed=4)
     e0 = torch.cuda.Event(enable_timing=True)
@@ -552,14 +553,23 @@ def measure_long(args, world, rank, local, ctx, K, W, check=False):
         step(i)
     ctx.sync()
     t0 = first + W
-    graph = None
+    graph = align = None
     if world > 1:
+        # One untimed step in a graph of its own is replayed first: the ranks' replays start at
+        # different host times, and that step's exchange (each rank waits for every rank's
+        # partials) absorbs the skew, so the events around the second graph time K steps of
+        # aligned ranks.
+        align = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(align):
+            step(t0)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            for i in range(t0, t0 + K):
+            for i in range(t0 + 1, t0 + 1 + K):
                 step(i)
+        align.replay()
         graph.replay()
         torch.cuda.synchronize()
+        t0 += 1
     # split-pass timing (events between the kernels) on steps of their own, before the timed ones
     barrier(torch, dist, world)
     ctx.set_timing(True)
@@ -573,18 +583,21 @@ def measure_long(args, world, rank, local, ctx, K, W, check=False):
     barrier(torch, dist, world)
     sampler = ClockSampler(local)
     sampler.start()
-    e0.record()
     if graph is not None:
+        align.replay()
+        e0.record()
         graph.replay()
+        e1.record()
     else:
+        e0.record()
         for i in range(t0, t0 + K):
             step(i)
-    e1.record()
+        e1.record()
     torch.cuda.synchronize()
     sampler.stop()
     rc = ctx.sync()
     ms = barrier_max(torch, dist, world, e0.elapsed_time(e1))
-    del graph
+    del graph, align
     torch.cuda.synchronize()
     # algorithmic bytes of this rank's split launches: its own share of the mean context
     mean_ctx = L + t0 + K // 2
