@@ -57,6 +57,30 @@ def test_append_edge_values_bit_exact(ctx):
     assert np.array_equal(vb, oracle.q8_quantize(toks[::-1].copy()))
 
 
+@pytest.mark.parametrize("n_kv,hd,T", [(3, 96, 7), (1, 32, 1), (5, 160, 13)])
+def test_append_odd_shapes_bit_exact(ctx, n_kv, hd, T):
+    """Blocks per token and tokens per entry that are not powers of two (the append divides
+    block indices by both), and blocks whose scale rounds down to a binary16 subnormal, where
+    |x / scale| exceeds 127.5 and the codes clamp at +-127."""
+    rng = np.random.default_rng(13 + n_kv)
+    n_seq, cap, B = 6, 40, 5
+    pool = vxg_b200.KvQ8Pool(ctx, n_seq, n_kv, hd, cap)
+    seq = rng.choice(n_seq, B, replace=False).astype(np.int32)
+    pos = rng.integers(0, cap - T, B).astype(np.int32)
+    k = rng.standard_normal((B, T, n_kv, hd)).astype(np.float32)
+    v = rng.standard_normal((B, T, n_kv, hd)).astype(np.float32)
+    # max |x| / 127 = 8.9e-8 rounds to the subnormal 5.96e-8: codes of -amax would be -190
+    tiny = np.linspace(-1.1303e-5, 2e-6, 32, dtype=np.float32)
+    k[0, 0, 0, :32] = tiny
+    v[-1, -1, -1, -32:] = -tiny[::-1]
+    pool.append(seq, pos, k, v, n_tok=T)
+    for b in range(B):
+        kb, vb = pool.export_blocks(int(seq[b]), int(pos[b]), T)
+        assert np.array_equal(kb, oracle.q8_quantize(k[b])), b
+        assert np.array_equal(vb, oracle.q8_quantize(v[b])), b
+    pool.close()
+
+
 def test_append_rejects_out_of_range(ctx):
     pool = vxg_b200.KvQ8Pool(ctx, 2, 2, 256, 8)
     k = np.zeros((1, 1, 2, 256), np.float32)
