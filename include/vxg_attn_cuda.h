@@ -153,7 +153,10 @@ VXG_ATTN_API int vxg_attn_cuda_q8_append(void* ctx, void* kv, uint32_t n_batch, 
  * q[b] ([n_head][head_dim] f32, already normed / RoPE'd) attends to tokens [0, pos[b]] with
  * softmax scale `scale` (1/sqrt(head_dim) in the reference).  q_gate (nullable, same shape as q)
  * applies out *= sigmoid(gate) (llm_prefill.rs:363-368).  out: [n_batch][n_head][head_dim].
- * max_ctx: an upper bound of pos[b] + 1 (0 = the pool capacity). */
+ * max_ctx: an upper bound of pos[b] + 1 (0 = the pool capacity).
+ * The KV ranges are split across the SMs in proportion to the rates the previous call of the
+ * context measured (batches of two or more entries), so two identical calls can sum a query's
+ * partials in a different order and differ in the last bits (within the accuracy bound). */
 VXG_ATTN_API int vxg_attn_cuda_q8_decode(void* ctx, void* kv, uint32_t n_batch, uint32_t n_head,
                             const int32_t* seq_ids, const int32_t* pos, const float* q,
                             const float* k_new, const float* v_new, const float* q_gate,
