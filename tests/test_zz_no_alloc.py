@@ -74,7 +74,8 @@ def _scratch_bytes_16_2_256(n, sm_count):
     a small batch, and the unit prefix plus CTA ranges."""
     grid = min(sm_count, 512)
     floats = (grid + n) * 6 * 16 * 258
-    splits = max(1, min(32, -(-128 // (4 * n))))
+    per = n * (8 if n < 32 else 4)  # combine CTAs per split level (32- or 64-dim chunks)
+    splits = max(1, min(32, -(-128 // per)))
     if splits > 1:
         floats += n * splits * 16 * 258
     return 4 * (1056 + floats + n + grid + 64)  # + the split pass's state (rates per CTA)

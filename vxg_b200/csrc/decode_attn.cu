@@ -955,15 +955,18 @@ __global__ void __launch_bounds__(256) decode_combine(DecodeArgs a, Partials par
 // (m, l, o) that decode_fast_combine_final merges.
 namespace {
 constexpr int kCombineSplitMax = 32;
-constexpr int kCombineDims = 64;
-constexpr int kCombineLanes = 4;   // slot lanes per output dim
 constexpr int kCombineStage = 128; // slots whose m / l / factors are staged at a time
 }
+// DIMS output dims per CTA, 256 / DIMS slot lanes per output dim: 64 dims for batches of 32
+// entries or more, 32 (twice the CTAs per entry) for smaller ones.
+template <int DIMS>
 __global__ void __launch_bounds__(256) decode_fast_combine(DecodeArgs a, Partials part, int n_cta,
                                                            int S, const float* gate, float* out,
                                                            float* m_out, float* l_out,
                                                            float* o_out) {
   using namespace fast;
+  constexpr int kCombineDims = DIMS;
+  constexpr int kCombineLanes = 256 / DIMS;
   constexpr int H = NKV * G;
   constexpr int MAXS = 512 + SUBS;  // one merged slot per CTA but the last (grid <= 512)
   grid_dep_wait();  // the split pass's partials and published ranges
@@ -1245,9 +1248,11 @@ int generic_max_split(const DecodeArgs& a) {
 namespace {
 // CTAs of the persistent split pass (the combine stages their unit ranges: at most 512).
 int fast_grid(int sm_count) { return std::max(1, std::min(fast::CPS * sm_count, 512)); }
-// Slot splits of the fast combine: aim for >= 128 CTAs of 64 output dims each.
+// Output dims per combine CTA (see decode_fast_combine), and its slot splits: aim for >= 128
+// CTAs per split level.
+int combine_dims(const DecodeArgs& a) { return a.n_batch < 32 ? 32 : 64; }
 int combine_splits(const DecodeArgs& a) {
-  const int per = std::max(1, a.n_batch * (fast::HD / kCombineDims));
+  const int per = std::max(1, a.n_batch * (fast::HD / combine_dims(a)));
   return std::max(1, std::min(kCombineSplitMax, (128 + per - 1) / per));
 }
 }  // namespace
@@ -1288,11 +1293,14 @@ namespace {
 cudaError_t launch_fast_combine(const DecodeArgs& a, const Partials& part, int sm_count,
                                 const float* gate, float* out, float* m_out, float* l_out,
                                 float* o_out, cudaStream_t st) {
-  const int S = combine_splits(a);
-  cudaError_t e = launch_dependent(decode_fast_combine,
-                                   dim3(a.n_batch, fast::HD / kCombineDims, S), dim3(256), 0, st,
-                                   a, part, fast_grid(sm_count), S, gate, out, m_out, l_out,
-                                   o_out);
+  const int S = combine_splits(a), dims = combine_dims(a);
+  cudaError_t e =
+      dims == 32 ? launch_dependent(decode_fast_combine<32>, dim3(a.n_batch, fast::HD / 32, S),
+                                    dim3(256), 0, st, a, part, fast_grid(sm_count), S, gate, out,
+                                    m_out, l_out, o_out)
+                 : launch_dependent(decode_fast_combine<64>, dim3(a.n_batch, fast::HD / 64, S),
+                                    dim3(256), 0, st, a, part, fast_grid(sm_count), S, gate, out,
+                                    m_out, l_out, o_out);
   if (e != cudaSuccess || S == 1) return e;
   return launch_dependent(decode_fast_combine_final, dim3(a.n_batch, fast::NKV * fast::G),
                           dim3(fast::HD), 0, st, a, part, S, gate, out, m_out, l_out, o_out);
